@@ -1,0 +1,248 @@
+"""``CustomAllreduce``: the idiomatic b200ar communicator.
+
+One object per rank (one process per GPU). Construction is collective over a
+``torch.distributed`` group: it allocates this rank's workspace (signal block +
+two message slots) with ``cudaMalloc``, exchanges CUDA IPC handles with
+``all_gather_object``, maps the peers' workspaces and builds the native
+communicator. This is the bootstrap that every reference script duplicates by
+hand (test_pcie_ar.py:25-65, stress_test.py:26-77, bench_crossover.py:29-94).
+
+For CPU tensors (``device="cpu"``) the same API runs on the shared-memory
+emulation of the protocol (``_C.ShmComm``), bootstrapped over a gloo group.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import uuid
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from .._native import _C
+from ..config import Config, default_config
+from ..log import logger
+from . import selector as sel
+
+CommTimeoutError = getattr(_C, "CommTimeout", RuntimeError)
+
+
+class CustomAllreduce:
+    """Sum all-reduce over NVLink/NVSwitch with custom sm_100a kernels.
+
+    Args:
+        group: process group used for bootstrap (handle exchange). Any backend
+            that supports object collectives (gloo recommended).
+        device: this rank's device (``torch.device``/index/``"cpu"``).
+        nccl_group: optional NCCL group for the large-message fallback. When
+            absent and ``group`` is an NCCL group, ``group`` is used.
+        config: ``Config``; keyword overrides (``max_size=...``) are accepted too.
+    """
+
+    def __init__(self, group=None, device=None, nccl_group=None, config: Optional[Config] = None, **overrides):
+        self.cfg = (config or default_config()).replace(**overrides) if overrides else (config or default_config())
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else "cpu"
+        self.device = torch.device(device) if not isinstance(device, int) else torch.device("cuda", device)
+        if nccl_group is None and group is not None and dist.get_backend(group) == "nccl":
+            nccl_group = group
+        if nccl_group is None and group is None and dist.is_initialized() and dist.get_backend() == "nccl":
+            nccl_group = dist.group.WORLD
+        self.nccl_group = nccl_group
+        self.closed = False
+        self._peer_ptrs: List[int] = []
+        self._ws_ptr = 0
+        self.nvls = None
+
+        # Slot capacity: two-shot of max_size, or one-shot push of push_max_size.
+        cap = max(
+            _C.variant_slot_bytes(sel.VARIANTS["twoshot"], self.cfg.max_size, self.world),
+            _C.variant_slot_bytes(sel.VARIANTS["oneshot_push"], self.cfg.push_max_size, self.world),
+            _C.variant_slot_bytes(sel.VARIANTS["oneshot_pull"], self.cfg.max_size, self.world),
+            4096,
+        )
+        self.slot_capacity = (cap + 255) // 256 * 256
+
+        if self.device.type == "cpu":
+            self._init_cpu()
+        else:
+            self._init_cuda()
+        self.set_selector(sel.load_table(self.world, self.cfg.selector_path or None))
+
+    # ------------------------------------------------------------------ setup
+    def _init_cpu(self) -> None:
+        token = [uuid.uuid4().hex[:12] if self.rank == 0 else None]
+        dist.broadcast_object_list(token, src=dist.get_global_rank(self.group, 0) if self.group else 0,
+                                   group=self.group)
+        self._shm = _C.ShmComm(f"/b200ar-{token[0]}", self.rank, self.world, self.slot_capacity)
+        names: List[Optional[str]] = [None] * self.world
+        dist.all_gather_object(names, self._shm.segment_name, group=self.group)
+        self._shm.connect(names)
+        self._shm.set_timeout_ms(self.cfg.timeout_ms)
+        dist.barrier(group=self.group)
+        self._comm = None
+
+    def _init_cuda(self) -> None:
+        self._shm = None
+        with torch.cuda.device(self.device):
+            ws_bytes = _C.workspace_bytes(self.slot_capacity)
+            self._ws_ptr = _C.ipc_malloc(ws_bytes)
+            handle = _C.ipc_get_handle(self._ws_ptr)
+            handles: List[Optional[bytes]] = [None] * self.world
+            dist.all_gather_object(handles, handle, group=self.group)
+            ptrs = []
+            for i, h in enumerate(handles):
+                ptrs.append(self._ws_ptr if i == self.rank else int(_C.ipc_open_handle(h)))
+            self._peer_ptrs = ptrs
+            self._rank_data = torch.empty(self.cfg.rank_data_bytes, dtype=torch.uint8, device=self.device)
+            self._comm = _C.Comm(ptrs, self._rank_data, self.rank)
+            sig = int(_C.SIGNAL_BYTES)
+            self._comm.register_slots(
+                [p + sig for p in ptrs], [p + sig + self.slot_capacity for p in ptrs], self.slot_capacity
+            )
+            self._comm.set_timeout_ns(int(self.cfg.timeout_ms) * 1_000_000)
+            torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        logger.info("rank %d: workspace %d bytes, slot capacity %d", self.rank, ws_bytes, self.slot_capacity)
+
+    # -------------------------------------------------------------- selection
+    def set_selector(self, entries) -> None:
+        self.selector = list(entries)
+        if self._comm is not None:
+            self._comm.set_selector(sel.to_native(self.selector))
+
+    def plan(self, nbytes: int, variant="auto", ctas: int = 0):
+        """(variant name, ctas, threads) that a message of ``nbytes`` would use."""
+        if self._comm is None:
+            return ("cpu", ctas, 0)
+        v, c, t = self._comm.plan(int(nbytes), sel.variant_id(variant), int(ctas))
+        return (sel.VARIANT_NAMES[v], c, t)
+
+    def supports(self, t: torch.Tensor) -> bool:
+        """True when ``t`` can be served by the custom kernels (else NCCL)."""
+        nbytes = t.numel() * t.element_size()
+        return (
+            t.dtype in (torch.float32, torch.float16, torch.bfloat16)
+            and nbytes % 16 == 0
+            and t.data_ptr() % 16 == 0
+            and t.is_contiguous()
+        )
+
+    # ------------------------------------------------------------ collectives
+    def all_reduce(self, inp: torch.Tensor, out: Optional[torch.Tensor] = None, variant="auto",
+                   ctas: int = 0) -> torch.Tensor:
+        """Returns the elementwise sum of ``inp`` over all ranks (``out`` may alias ``inp``)."""
+        if self.closed:
+            raise RuntimeError("communicator is closed")
+        if out is None:
+            out = torch.empty_like(inp)
+        v = sel.variant_id(variant if variant != "auto" else self.cfg.variant)
+        if self._comm is None:
+            self._shm.all_reduce(inp, out, v, ctas)
+            return out
+        if not self.supports(inp) or not self.supports(out) or v == sel.VARIANTS["nccl"]:
+            return self._nccl(inp, out)
+        launched = self._comm.all_reduce(inp, out, v, ctas)
+        if launched == sel.VARIANTS["nccl"]:
+            return self._nccl(inp, out)
+        return out
+
+    def _nccl(self, inp: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        if self.nccl_group is None:
+            raise RuntimeError(
+                "message cannot be served by the custom kernels (size/alignment/capacity) and no NCCL group "
+                "was given for the fallback"
+            )
+        if out.data_ptr() != inp.data_ptr():
+            out.copy_(inp)
+        dist.all_reduce(out, group=self.nccl_group)
+        return out
+
+    # ----------------------------------------------- registered buffers / graphs
+    def register_buffer(self, t: torch.Tensor) -> None:
+        """Registers ``t`` (allocated by ``cudaMalloc``-backed memory, e.g.
+        ``b200ar.ipc.CudaIPC().malloc``) for the zero-copy variant: collective."""
+        ptrs = exchange_ptr(t.data_ptr(), self.group)
+        self._comm.register_buffer(ptrs)
+
+    @contextlib.contextmanager
+    def capture(self):
+        """Context for capturing a CUDA graph that uses the zero-copy
+        ``variant="registered"`` path: on exit, the input addresses recorded
+        during capture are exchanged and registered (collective). Calls that use
+        the slot variants need no registration and work in graphs as they are."""
+        try:
+            yield self
+        finally:
+            self.register_graph_buffers()
+
+    def register_graph_buffers(self) -> None:
+        if self._comm is None:
+            return
+        handles, offsets = self._comm.graph_buffer_meta()
+        meta: List[Optional[tuple]] = [None] * self.world
+        dist.all_gather_object(meta, (handles, offsets), group=self.group)
+        self._comm.register_graph_buffers([m[0] for m in meta], [m[1] for m in meta])
+
+    # ------------------------------------------------------- status and reset
+    def check(self) -> None:
+        """Raises ``CommTimeoutError`` if a kernel reported a barrier timeout."""
+        if self._comm is not None:
+            self._comm.check()
+
+    def status(self) -> dict:
+        return self._comm.status() if self._comm is not None else {"code": self._shm.status_code()}
+
+    def reset(self) -> None:
+        """Collective recovery after a timeout: every rank zeroes its signal
+        block between two barriers of the bootstrap group."""
+        if self._comm is not None:
+            torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        if self._comm is not None:
+            self._comm.reset()
+        else:
+            self._shm.reset()
+        dist.barrier(group=self.group)
+
+    @property
+    def launches(self) -> int:
+        """Number of kernels launched by this communicator so far."""
+        return self._comm.launches if self._comm is not None else 0
+
+    def close(self) -> None:
+        """Collective teardown: waits until no peer can still touch this rank's
+        workspace (device sync + group barrier), then unmaps and frees it."""
+        if self.closed:
+            return
+        self.closed = True
+        if self._comm is not None:
+            torch.cuda.synchronize(self.device)
+        if dist.is_initialized():
+            dist.barrier(group=self.group)
+        if self._comm is not None:
+            del self._comm
+            self._comm = None
+            for i, p in enumerate(self._peer_ptrs):
+                if i != self.rank:
+                    _C.ipc_close_handle(p)
+            if self._ws_ptr:
+                _C.ipc_free(self._ws_ptr)
+                self._ws_ptr = 0
+        self._shm = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+def exchange_ptr(ptr: int, group=None) -> List[int]:
+    from ..ipc import exchange_buffers
+
+    return exchange_buffers(ptr, group)

@@ -1,0 +1,56 @@
+// Instantiation and dispatch of the all-reduce kernels (ar_kernels.cuh) over
+// dtype {fp32, fp16, bf16} x world size {2..8} x variant. The reference
+// instantiated world sizes {2, 4, 6, 8} only (pcie_allreduce.cu:427-433);
+// NVSwitch gives every rank count the same topology, so odd sizes are served too.
+#include <stdexcept>
+#include <string>
+
+#include "../common/check.h"
+#include "ar_kernels.cuh"
+
+namespace b200ar {
+
+namespace {
+
+template <typename T, int N>
+void launch_typed(int variant, int ctas, int threads, const ArArgs& a, cudaStream_t s) {
+  switch (variant) {
+    case kOneshotPush: oneshot_push_kernel<T, N><<<ctas, threads, 0, s>>>(a); break;
+    case kOneshotPull: oneshot_pull_kernel<T, N><<<ctas, threads, 0, s>>>(a); break;
+    case kTwoshot: twoshot_kernel<T, N><<<ctas, threads, 0, s>>>(a); break;
+    case kRegistered: registered_kernel<T, N><<<ctas, threads, 0, s>>>(a); break;
+    default: throw std::invalid_argument("unknown all-reduce variant " + std::to_string(variant));
+  }
+}
+
+template <typename T>
+void launch_world(int variant, int world, int ctas, int threads, const ArArgs& a, cudaStream_t s) {
+  switch (world) {
+    case 2: launch_typed<T, 2>(variant, ctas, threads, a, s); break;
+    case 3: launch_typed<T, 3>(variant, ctas, threads, a, s); break;
+    case 4: launch_typed<T, 4>(variant, ctas, threads, a, s); break;
+    case 5: launch_typed<T, 5>(variant, ctas, threads, a, s); break;
+    case 6: launch_typed<T, 6>(variant, ctas, threads, a, s); break;
+    case 7: launch_typed<T, 7>(variant, ctas, threads, a, s); break;
+    case 8: launch_typed<T, 8>(variant, ctas, threads, a, s); break;
+    default: throw std::invalid_argument("unsupported world size " + std::to_string(world));
+  }
+}
+
+}  // namespace
+
+void launch_ar_kernel(int variant, DType dt, int world, int ctas, int threads, const ArArgs& a,
+                      cudaStream_t stream) {
+  if (ctas < 1 || ctas > kMaxCTAs) throw std::invalid_argument("bad CTA count " + std::to_string(ctas));
+  if (threads < 32 || threads > kArThreads || threads % 32 != 0)
+    throw std::invalid_argument("bad thread count " + std::to_string(threads));
+  switch (dt) {
+    case DType::kFloat32: launch_world<float>(variant, world, ctas, threads, a, stream); break;
+    case DType::kFloat16: launch_world<__half>(variant, world, ctas, threads, a, stream); break;
+    case DType::kBFloat16: launch_world<__nv_bfloat16>(variant, world, ctas, threads, a, stream); break;
+    default: throw std::invalid_argument("only float32, float16 and bfloat16 are supported");
+  }
+  B200AR_CUDA(cudaGetLastError());
+}
+
+}  // namespace b200ar

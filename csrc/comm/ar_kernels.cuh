@@ -1,0 +1,245 @@
+// All-reduce kernels of b200ar for sm_100a (sum, fp32 accumulation).
+//
+// All kernels are multi-CTA; CTA j of every rank works on the same packet range
+// and synchronises only with CTA j of the peers (per-CTA flags), so the ranks
+// must launch identical grids for the same call. Data moves as 16-byte packets
+// with P2P loads/stores over NVLink to peer HBM mapped with CUDA IPC.
+//
+// Variants (kernel <-> reference kernel):
+//  * oneshot_push  <-> fused_push_reduce_kernel (pcie_allreduce.cu:182-220):
+//    push own input into every rank's slot[rank], barrier, reduce locally.
+//    The reference runs it on a single CTA; here every CTA pushes its chunk.
+//  * oneshot_pull  <-> fused_pull_reduce_kernel (cu:227-257): copy-in fused,
+//    barrier, rotated pull-reduce from every peer.
+//  * twoshot (new): push-reduce-scatter, barrier, reduce own part, barrier,
+//    pull-all-gather. Moves 2(N-1)/N of the message per direction per rank.
+//  * registered    <-> pcie_allreduce_kernel (cu:261-276): pull directly from
+//    registered peer buffers. Adds the end barrier the reference lacks, so a
+//    rank cannot overwrite its input while a peer still reads it.
+#pragma once
+
+#include "../common/device.cuh"
+
+namespace b200ar {
+
+constexpr int kArThreads = 512;
+
+// Peer pointers of registered user buffers, stored in device memory so that
+// CUDA-graph captures can reference a slot that is filled after capture.
+struct alignas(16) RankData {
+  const void* ptrs[kMaxRanks];
+};
+
+struct ArArgs {
+  CommCtx ctx;
+  char* slot[2][kMaxRanks];  // base of slot s on every rank (peer mappings)
+  const char* in;            // local input
+  char* out;                 // local output
+  const RankData* rd;        // registered variant only
+  int64_t packets;           // message size in 16-byte packets
+};
+
+// Fills d[k] = base[(rank + k) % N] without dynamic indexing of a local array.
+template <int N>
+B200AR_DEV void rotate_ptrs(char* const* base, int rank, char** d) {
+#pragma unroll
+  for (int k = 0; k < N; ++k) {
+    char* v = nullptr;
+    const int want = (rank + k) % N;
+#pragma unroll
+    for (int p = 0; p < N; ++p)
+      if (p == want) v = base[p];
+    d[k] = v;
+  }
+}
+
+template <typename T, int N>
+__global__ void __launch_bounds__(kArThreads) oneshot_push_kernel(ArArgs a) {
+  __shared__ uint32_t s_gen;
+  const uint32_t gen = read_generation(a.ctx, &s_gen);
+  const int slot = gen & 1u;
+  const int r = a.ctx.rank;
+  const int64_t P = a.packets;
+  const int64_t b = part_begin(P, gridDim.x, blockIdx.x);
+  const int64_t e = part_begin(P, gridDim.x, blockIdx.x + 1);
+
+  char* dst[N];
+  rotate_ptrs<N>(a.slot[slot], r, dst);
+  const int64_t my_off = static_cast<int64_t>(r) * P * 16;
+
+  for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) {
+    const uint4 v = ld_in(a.in + i * 16);
+#pragma unroll
+    for (int k = 0; k < N; ++k) st_cg(dst[k] + my_off + i * 16, v);
+  }
+
+  if (cta_barrier<N>(a.ctx, blockIdx.x, epoch_of(gen, 0))) {
+    const char* mine = a.slot[slot][r];
+    for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) {
+      uint4 v[N];
+#pragma unroll
+      for (int q = 0; q < N; ++q) v[q] = ld_cg(mine + (static_cast<int64_t>(q) * P + i) * 16);
+      float acc[PackTraits<T>::kElems];
+      unpack_set<T>(v[0], acc);
+#pragma unroll
+      for (int q = 1; q < N; ++q) unpack_add<T>(v[q], acc);
+      st_out(a.out + i * 16, pack<T>(acc));
+    }
+  }
+  finish_generation(a.ctx, gen);
+}
+
+template <typename T, int N>
+__global__ void __launch_bounds__(kArThreads) oneshot_pull_kernel(ArArgs a) {
+  __shared__ uint32_t s_gen;
+  const uint32_t gen = read_generation(a.ctx, &s_gen);
+  const int slot = gen & 1u;
+  const int r = a.ctx.rank;
+  const int64_t P = a.packets;
+  const int64_t b = part_begin(P, gridDim.x, blockIdx.x);
+  const int64_t e = part_begin(P, gridDim.x, blockIdx.x + 1);
+
+  // Peers are summed in rank order 0..N-1 on every rank, so all ranks get
+  // bitwise identical results (the reference rotated the order per rank,
+  // pcie_allreduce.cu:248-253, which makes results rank dependent).
+  char* const* src = a.slot[slot];
+  char* mine = src[r];
+  for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) st_cg(mine + i * 16, ld_in(a.in + i * 16));
+
+  if (cta_barrier<N>(a.ctx, blockIdx.x, epoch_of(gen, 0))) {
+    for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) {
+      uint4 v[N];
+#pragma unroll
+      for (int k = 0; k < N; ++k) v[k] = ld_cg(src[k] + i * 16);
+      float acc[PackTraits<T>::kElems];
+      unpack_set<T>(v[0], acc);
+#pragma unroll
+      for (int k = 1; k < N; ++k) unpack_add<T>(v[k], acc);
+      st_out(a.out + i * 16, pack<T>(acc));
+    }
+  }
+  finish_generation(a.ctx, gen);
+}
+
+// Two-shot. Slot layout on every rank (in packets, part = ceil(P / N)):
+//   [0, N*part)        reduce-scatter inbox, row q holds rank q's copy of this rank's part
+//   [N*part, (N+1)*part) all-gather outbox: this rank's reduced part
+template <typename T, int N>
+__global__ void __launch_bounds__(kArThreads) twoshot_kernel(ArArgs a) {
+  __shared__ uint32_t s_gen;
+  const uint32_t gen = read_generation(a.ctx, &s_gen);
+  const int slot = gen & 1u;
+  const int r = a.ctx.rank;
+  const int64_t P = a.packets;
+  const int64_t part = (P + N - 1) / N;
+  const int G = gridDim.x;
+  const int j = blockIdx.x;
+
+  char* peer[N];  // peer[k] = slot base of rank (r + k) % N
+  rotate_ptrs<N>(a.slot[slot], r, peer);
+
+  // Sub-range of part p = (r + k) % N handled by this CTA: absolute packet
+  // start ab[k], start relative to the part rb[k], length ln[k].
+  int64_t ab[N];
+  int rb[N], ln[N];
+  int smax = 0;
+#pragma unroll
+  for (int k = 0; k < N; ++k) {
+    const int p = (r + k) % N;
+    const int64_t pb = part_begin(P, N, p);
+    const int64_t plen = part_begin(P, N, p + 1) - pb;
+    const int64_t sb = part_begin(plen, G, j);
+    rb[k] = static_cast<int>(sb);
+    ln[k] = static_cast<int>(part_begin(plen, G, j + 1) - sb);
+    ab[k] = pb + sb;
+    smax = ln[k] > smax ? ln[k] : smax;
+  }
+
+  // Phase 1: scatter. Rank r's copy of part p goes to row r of p's inbox.
+  const int64_t row = static_cast<int64_t>(r) * part;
+  for (int o = threadIdx.x; o < smax; o += blockDim.x) {
+    uint4 v[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k)
+      if (o < ln[k]) v[k] = ld_in(a.in + (ab[k] + o) * 16);
+#pragma unroll
+    for (int k = 0; k < N; ++k)
+      if (o < ln[k]) st_cg(peer[k] + (row + rb[k] + o) * 16, v[k]);
+  }
+
+  bool ok = cta_barrier<N>(a.ctx, j, epoch_of(gen, 0));
+
+  // Phase 2: reduce own part (k == 0), write result to output and outbox.
+  if (ok) {
+    char* mine = peer[0];
+    for (int o = threadIdx.x; o < ln[0]; o += blockDim.x) {
+      const int64_t rel = rb[0] + o;
+      uint4 v[N];
+#pragma unroll
+      for (int q = 0; q < N; ++q) v[q] = ld_cg(mine + (static_cast<int64_t>(q) * part + rel) * 16);
+      float acc[PackTraits<T>::kElems];
+      unpack_set<T>(v[0], acc);
+#pragma unroll
+      for (int q = 1; q < N; ++q) unpack_add<T>(v[q], acc);
+      const uint4 res = pack<T>(acc);
+      st_out(a.out + (ab[0] + o) * 16, res);
+      st_cg(mine + (static_cast<int64_t>(N) * part + rel) * 16, res);
+    }
+  }
+
+  ok = cta_barrier<N>(a.ctx, j, epoch_of(gen, 1)) && ok;
+
+  // Phase 3: gather reduced parts of the peers.
+  if (ok) {
+    const int64_t outbox = static_cast<int64_t>(N) * part;
+    for (int o = threadIdx.x; o < smax; o += blockDim.x) {
+      uint4 v[N];
+#pragma unroll
+      for (int k = 1; k < N; ++k)
+        if (o < ln[k]) v[k] = ld_cg(peer[k] + (outbox + rb[k] + o) * 16);
+#pragma unroll
+      for (int k = 1; k < N; ++k)
+        if (o < ln[k]) st_out(a.out + (ab[k] + o) * 16, v[k]);
+    }
+  }
+  finish_generation(a.ctx, gen);
+}
+
+// Pull-reduce straight from registered peer buffers (no staging copy).
+template <typename T, int N>
+__global__ void __launch_bounds__(kArThreads) registered_kernel(ArArgs a) {
+  __shared__ uint32_t s_gen;
+  __shared__ const char* s_ptr[kMaxRanks];
+  const uint32_t gen = read_generation(a.ctx, &s_gen);
+  if (threadIdx.x < N) s_ptr[threadIdx.x] = static_cast<const char*>(a.rd->ptrs[threadIdx.x]);  // rank order
+  const int64_t P = a.packets;
+  const int64_t b = part_begin(P, gridDim.x, blockIdx.x);
+  const int64_t e = part_begin(P, gridDim.x, blockIdx.x + 1);
+
+  if (cta_barrier<N>(a.ctx, blockIdx.x, epoch_of(gen, 0))) {
+    const char* src[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k) src[k] = s_ptr[k];
+    for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) {
+      uint4 v[N];
+#pragma unroll
+      for (int k = 0; k < N; ++k) v[k] = ld_cg(src[k] + i * 16);
+      float acc[PackTraits<T>::kElems];
+      unpack_set<T>(v[0], acc);
+#pragma unroll
+      for (int k = 1; k < N; ++k) unpack_add<T>(v[k], acc);
+      st_out(a.out + i * 16, pack<T>(acc));
+    }
+  }
+  // End barrier: no rank leaves (and overwrites its input) while peers read it.
+  cta_barrier<N>(a.ctx, blockIdx.x, epoch_of(gen, 1));
+  finish_generation(a.ctx, gen);
+}
+
+}  // namespace b200ar
+
+namespace b200ar {
+// Host launcher for the kernels above (ar_kernels.cu).
+void launch_ar_kernel(int variant, DType dt, int world, int ctas, int threads, const ArArgs& args,
+                      cudaStream_t stream);
+}  // namespace b200ar

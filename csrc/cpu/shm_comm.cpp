@@ -1,0 +1,254 @@
+// CPU shared-memory backend (see shm_comm.h).
+#include "shm_comm.h"
+
+#include <c10/util/BFloat16.h>
+#include <c10/util/Half.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <unistd.h>
+
+#include <atomic>
+#include <chrono>
+#include <cstring>
+#include <sstream>
+#include <stdexcept>
+#include <thread>
+
+#include "../common/check.h"
+
+namespace b200ar {
+
+namespace {
+
+inline void st_release(uint32_t* p, uint32_t v) { __atomic_store_n(p, v, __ATOMIC_RELEASE); }
+inline uint32_t ld_acquire(const uint32_t* p) { return __atomic_load_n(p, __ATOMIC_ACQUIRE); }
+
+template <typename T>
+inline float to_f(T v) {
+  return static_cast<float>(v);
+}
+template <typename T>
+inline T from_f(float v) {
+  return static_cast<T>(v);  // c10::BFloat16 / c10::Half round to nearest even
+}
+
+template <typename T>
+constexpr int elems() {
+  return 16 / static_cast<int>(sizeof(T));
+}
+
+template <typename T>
+inline void packet_set(const char* p, float* acc) {
+  const T* e = reinterpret_cast<const T*>(p);
+  for (int i = 0; i < elems<T>(); ++i) acc[i] = to_f(e[i]);
+}
+template <typename T>
+inline void packet_add(const char* p, float* acc) {
+  const T* e = reinterpret_cast<const T*>(p);
+  for (int i = 0; i < elems<T>(); ++i) acc[i] += to_f(e[i]);
+}
+template <typename T>
+inline void packet_store(char* p, const float* acc) {
+  T* e = reinterpret_cast<T*>(p);
+  for (int i = 0; i < elems<T>(); ++i) e[i] = from_f<T>(acc[i]);
+}
+
+}  // namespace
+
+ShmComm::ShmComm(const std::string& prefix, int rank, int world, int64_t slot_capacity)
+    : rank_(rank), world_(world), cap_(slot_capacity), names_(world), base_(world, nullptr) {
+  B200AR_CHECK(world >= 1 && world <= kMaxRanks, "world size must be in [1, " << kMaxRanks << "]");
+  B200AR_CHECK(rank >= 0 && rank < world, "invalid rank " << rank);
+  B200AR_CHECK(slot_capacity > 0 && slot_capacity % 16 == 0, "slot capacity must be a positive multiple of 16");
+  seg_bytes_ = workspace_bytes(cap_);
+  names_[rank] = prefix + "-r" + std::to_string(rank);
+  const int fd = shm_open(names_[rank].c_str(), O_CREAT | O_EXCL | O_RDWR, 0600);
+  if (fd < 0) throw std::runtime_error("shm_open(" + names_[rank] + ") failed: " + std::strerror(errno));
+  if (ftruncate(fd, seg_bytes_) != 0) {
+    close(fd);
+    shm_unlink(names_[rank].c_str());
+    throw std::runtime_error("ftruncate of shared segment failed");
+  }
+  void* p = mmap(nullptr, seg_bytes_, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
+  close(fd);
+  if (p == MAP_FAILED) {
+    shm_unlink(names_[rank].c_str());
+    throw std::runtime_error("mmap of shared segment failed");
+  }
+  std::memset(p, 0, sizeof(Signal));
+  base_[rank] = static_cast<char*>(p);
+}
+
+ShmComm::~ShmComm() {
+  for (int i = 0; i < world_; ++i)
+    if (base_[i]) munmap(base_[i], seg_bytes_);
+  if (!owner_unlinked_) shm_unlink(names_[rank_].c_str());
+}
+
+void ShmComm::connect(const std::vector<std::string>& names) {
+  B200AR_CHECK(static_cast<int>(names.size()) == world_, "need one segment name per rank");
+  B200AR_CHECK(names[rank_] == names_[rank_], "names[rank] must be this rank's own segment");
+  for (int i = 0; i < world_; ++i) {
+    if (i == rank_) continue;
+    const int fd = shm_open(names[i].c_str(), O_RDWR, 0600);
+    if (fd < 0) throw std::runtime_error("shm_open(" + names[i] + ") failed: " + std::strerror(errno));
+    void* p = mmap(nullptr, seg_bytes_, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
+    close(fd);
+    if (p == MAP_FAILED) throw std::runtime_error("mmap of peer segment failed");
+    base_[i] = static_cast<char*>(p);
+    names_[i] = names[i];
+  }
+}
+
+uint32_t ShmComm::generation() const { return ld_acquire(&reinterpret_cast<Signal*>(base_[rank_])->gen); }
+
+void ShmComm::reset() {
+  std::memset(base_[rank_], 0, sizeof(Signal));
+  std::atomic_thread_fence(std::memory_order_seq_cst);
+  status_ = Status{};
+  skip_ = 0;
+}
+
+bool ShmComm::barrier(int cta, uint32_t epoch) {
+  Signal* self = reinterpret_cast<Signal*>(base_[rank_]);
+  for (int p = 0; p < world_; ++p)
+    st_release(&reinterpret_cast<Signal*>(base_[p])->flags[cta][rank_], epoch);
+  const auto start = std::chrono::steady_clock::now();
+  for (int p = 0; p < world_; ++p) {
+    uint32_t seen;
+    uint32_t spins = 0;
+    while (!epoch_reached(seen = ld_acquire(&self->flags[cta][p]), epoch)) {
+      if ((++spins & 255u) == 0u) {
+        std::this_thread::yield();
+        const auto ms =
+            std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - start).count();
+        if (ms > timeout_ms_) {
+          if (status_.code == kStatusOk) {
+            status_.code = kStatusTimeout;
+            status_.rank = rank_;
+            status_.peer = p;
+            status_.cta = cta;
+            status_.epoch = epoch;
+            status_.seen = seen;
+          }
+          ++status_.count;
+          return false;
+        }
+      }
+    }
+  }
+  return true;
+}
+
+template <typename T>
+void ShmComm::run(const char* in, char* out, int64_t P, int variant, int G) {
+  Signal* self = reinterpret_cast<Signal*>(base_[rank_]);
+  const uint32_t gen = self->gen;
+  const int slot = gen & 1u;
+  const int N = world_;
+  const int r = rank_;
+  auto slotp = [&](int p) { return base_[p] + slot_offset(slot, cap_); };
+  constexpr int E = elems<T>();
+  float acc[E];
+  bool ok = true;
+  const bool skip = skip_ > 0;
+
+  for (int j = 0; j < G && ok; ++j) {
+    if (variant == kOneshotPush || variant == kOneshotPull) {
+      const int64_t b = part_begin(P, G, j), e = part_begin(P, G, j + 1);
+      if (variant == kOneshotPush) {
+        for (int64_t i = b; i < e; ++i)
+          for (int k = 0; k < N; ++k) {
+            const int p = (r + k) % N;
+            std::memcpy(slotp(p) + (static_cast<int64_t>(r) * P + i) * 16, in + i * 16, 16);
+          }
+      } else {
+        std::memcpy(slotp(r) + b * 16, in + b * 16, (e - b) * 16);
+      }
+      if (skip) continue;
+      if (!(ok = barrier(j, epoch_of(gen, 0)))) break;
+      for (int64_t i = b; i < e; ++i) {
+        if (variant == kOneshotPush) {
+          const char* mine = slotp(r);
+          packet_set<T>(mine + i * 16, acc);
+          for (int q = 1; q < N; ++q) packet_add<T>(mine + (static_cast<int64_t>(q) * P + i) * 16, acc);
+        } else {
+          packet_set<T>(slotp(0) + i * 16, acc);
+          for (int q = 1; q < N; ++q) packet_add<T>(slotp(q) + i * 16, acc);
+        }
+        packet_store<T>(out + i * 16, acc);
+      }
+    } else if (variant == kTwoshot) {
+      const int64_t part = (P + N - 1) / N;
+      auto sub = [&](int p, int64_t* pb, int64_t* sb, int64_t* sl) {
+        *pb = part_begin(P, N, p);
+        const int64_t plen = part_begin(P, N, p + 1) - *pb;
+        *sb = part_begin(plen, G, j);
+        *sl = part_begin(plen, G, j + 1) - *sb;
+      };
+      int64_t pb, sb, sl;
+      for (int k = 0; k < N; ++k) {
+        const int p = (r + k) % N;
+        sub(p, &pb, &sb, &sl);
+        std::memcpy(slotp(p) + (static_cast<int64_t>(r) * part + sb) * 16, in + (pb + sb) * 16, sl * 16);
+      }
+      if (skip) continue;
+      if (!(ok = barrier(j, epoch_of(gen, 0)))) break;
+      sub(r, &pb, &sb, &sl);
+      char* mine = slotp(r);
+      for (int64_t o = sb; o < sb + sl; ++o) {
+        packet_set<T>(mine + o * 16, acc);
+        for (int q = 1; q < N; ++q) packet_add<T>(mine + (static_cast<int64_t>(q) * part + o) * 16, acc);
+        packet_store<T>(out + (pb + o) * 16, acc);
+        std::memcpy(mine + (static_cast<int64_t>(N) * part + o) * 16, out + (pb + o) * 16, 16);
+      }
+      if (!(ok = barrier(j, epoch_of(gen, 1)))) break;
+      for (int k = 1; k < N; ++k) {
+        const int p = (r + k) % N;
+        sub(p, &pb, &sb, &sl);
+        std::memcpy(out + (pb + sb) * 16, slotp(p) + (static_cast<int64_t>(N) * part + sb) * 16, sl * 16);
+      }
+    } else {
+      throw std::invalid_argument("CPU backend supports variants push (1), pull (2) and two-shot (3)");
+    }
+  }
+  if (skip) --skip_;
+  __atomic_store_n(&self->gen, gen + 1u, __ATOMIC_RELEASE);
+  if (!ok) {
+    std::ostringstream os;
+    os << "b200ar(cpu): rank " << status_.rank << " timed out waiting for rank " << status_.peer << " (cta "
+       << status_.cta << ", epoch " << status_.epoch << ", last seen " << status_.seen << ")";
+    throw CommTimeout(os.str());
+  }
+}
+
+void ShmComm::allreduce(const void* in, void* out, int64_t bytes, DType dt, int variant, int ctas) {
+  B200AR_CHECK(bytes % 16 == 0, "all-reduce size must be a multiple of 16 bytes");
+  B200AR_CHECK(base_.size() == static_cast<size_t>(world_), "not connected");
+  for (int i = 0; i < world_; ++i) B200AR_CHECK(base_[i] != nullptr, "not connected to rank " << i);
+  if (status_.code != kStatusOk)
+    throw CommTimeout("b200ar(cpu): communicator is in error state; reset() it collectively");
+  if (bytes == 0) return;
+  if (world_ == 1) {
+    if (in != out) std::memmove(out, in, bytes);
+    return;
+  }
+  if (variant == kAuto) variant = bytes <= 256 * 1024 ? kOneshotPush : kTwoshot;
+  const int64_t need = variant_slot_bytes(variant, bytes, world_);
+  if (need > cap_) {
+    variant = variant_slot_bytes(kTwoshot, bytes, world_) <= cap_ ? kTwoshot : kOneshotPull;
+    B200AR_CHECK(variant_slot_bytes(variant, bytes, world_) <= cap_,
+                 "message of " << bytes << " bytes does not fit the slot capacity " << cap_);
+  }
+  const int64_t P = bytes / 16;
+  const int G = ctas > 0 ? std::min(ctas, kMaxCTAs) : 4;
+  const char* i = static_cast<const char*>(in);
+  char* o = static_cast<char*>(out);
+  switch (dt) {
+    case DType::kFloat32: run<float>(i, o, P, variant, G); break;
+    case DType::kFloat16: run<c10::Half>(i, o, P, variant, G); break;
+    case DType::kBFloat16: run<c10::BFloat16>(i, o, P, variant, G); break;
+  }
+}
+
+}  // namespace b200ar
