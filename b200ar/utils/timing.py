@@ -1,0 +1,73 @@
+"""Device timing helpers: CUDA-event timing, L2 flushing, max-over-ranks
+reduction and summary statistics.
+
+The reference timed with host ``time.perf_counter`` around a loop on each rank
+and printed rank 0 only (bench_crossover.py:113-134, 203-210). b200ar times each
+call with CUDA events on the launching stream and reduces every iteration's time
+with a MAX over ranks before taking percentiles.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Dict, List, Sequence
+
+import torch
+import torch.distributed as dist
+
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2 of B200
+
+
+class L2Flusher:
+    """Overwrites a buffer larger than L2 so the next kernel starts cold."""
+
+    def __init__(self, device, nbytes: int = L2_FLUSH_BYTES):
+        self.buf = torch.empty(nbytes // 4, dtype=torch.int32, device=device)
+
+    def __call__(self) -> None:
+        self.buf.fill_(0x5A5A5A5A)
+
+
+class EventTimer:
+    """Collects (start, end) CUDA event pairs keyed by name; ``times_ms`` syncs
+    once and returns every recorded duration."""
+
+    def __init__(self):
+        self.pairs: Dict[str, List] = {}
+
+    def start(self, key: str):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        self.pairs.setdefault(key, []).append([e, None])
+
+    def stop(self, key: str):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        self.pairs[key][-1][1] = e
+
+    def times_ms(self) -> Dict[str, List[float]]:
+        torch.cuda.synchronize()
+        return {k: [a.elapsed_time(b) for a, b in v] for k, v in self.pairs.items()}
+
+
+def max_over_ranks(values: Sequence[float], device, group=None) -> List[float]:
+    """Element-wise MAX of ``values`` over all ranks (identity without a process group)."""
+    if not (dist.is_initialized() and dist.get_world_size(group) > 1):
+        return list(values)
+    t = torch.tensor(list(values), dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return t.tolist()
+
+
+def percentile(values: Sequence[float], q: float) -> float:
+    v = sorted(values)
+    if not v:
+        return float("nan")
+    k = (len(v) - 1) * q / 100.0
+    lo, hi = math.floor(k), math.ceil(k)
+    return v[lo] + (v[hi] - v[lo]) * (k - lo)
+
+
+def geomean(values: Sequence[float]) -> float:
+    v = [x for x in values if x > 0]
+    return math.exp(sum(math.log(x) for x in v) / len(v)) if v else float("nan")

@@ -2,6 +2,7 @@
 // dtype {fp32, fp16, bf16} x world size {2..8} x variant. The reference
 // instantiated world sizes {2, 4, 6, 8} only (pcie_allreduce.cu:427-433);
 // NVSwitch gives every rank count the same topology, so odd sizes are served too.
+#include <algorithm>
 #include <stdexcept>
 #include <string>
 
@@ -37,7 +38,22 @@ void launch_world(int variant, int world, int ctas, int threads, const ArArgs& a
   }
 }
 
+// World size 1: the sum over one rank is the input itself (16-byte copy).
+__global__ void __launch_bounds__(kArThreads) copy_kernel(const char* __restrict__ in, char* __restrict__ out,
+                                                          int64_t packets) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < packets;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    st_out(out + i * 16, ld_in(in + i * 16));
+}
+
 }  // namespace
+
+void launch_copy(const void* in, void* out, int64_t packets, cudaStream_t stream) {
+  const int64_t want = std::max<int64_t>((packets + kArThreads - 1) / kArThreads, 1);
+  const int ctas = static_cast<int>(std::min<int64_t>(want, 4 * 148));
+  copy_kernel<<<ctas, kArThreads, 0, stream>>>(static_cast<const char*>(in), static_cast<char*>(out), packets);
+  B200AR_CUDA(cudaGetLastError());
+}
 
 void launch_ar_kernel(int variant, DType dt, int world, int ctas, int threads, const ArArgs& a,
                       cudaStream_t stream) {

@@ -242,4 +242,6 @@ namespace b200ar {
 // Host launcher for the kernels above (ar_kernels.cu).
 void launch_ar_kernel(int variant, DType dt, int world, int ctas, int threads, const ArArgs& args,
                       cudaStream_t stream);
+// World size 1: out = in (16-byte packets) with a b200ar kernel.
+void launch_copy(const void* in, void* out, int64_t packets, cudaStream_t stream);
 }  // namespace b200ar

@@ -294,7 +294,10 @@ LaunchInfo Communicator::allreduce(cudaStream_t stream, const void* in, void* ou
   li = plan(bytes, variant, ctas, capturing, registered_input);
   if (li.variant == kNccl) return li;
   if (li.variant == kCopy) {
-    if (in != out) B200AR_CUDA(cudaMemcpyAsync(out, in, bytes, cudaMemcpyDeviceToDevice, stream));
+    if (in != out) {
+      launch_copy(in, out, bytes / 16, stream);
+      ++launches_;
+    }
     return li;
   }
   B200AR_CHECK(li.variant != kNvls, "NVLS all-reduce is served by the NVLS communicator");
