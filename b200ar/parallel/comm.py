@@ -151,6 +151,27 @@ class CustomAllreduce:
             return self._nccl(inp, out)
         return out
 
+    def all_reduce_residual_rmsnorm(self, x: torch.Tensor, residual: torch.Tensor, gamma: torch.Tensor,
+                                    eps: float = 1e-5, out: Optional[torch.Tensor] = None,
+                                    residual_out: Optional[torch.Tensor] = None, variant="auto", ctas: int = 0):
+        """Fused TP decode epilogue: ``z = all_reduce(x) + residual``,
+        ``out = RMSNorm(z) * gamma``. Returns ``(out, z)``; ``residual_out`` may
+        alias ``residual`` (in-place residual update) and ``out`` may alias ``x``."""
+        if out is None:
+            out = torch.empty_like(x)
+        if residual_out is None:
+            residual_out = torch.empty_like(residual)
+        if self._comm is None:
+            z = self.all_reduce(x.float().contiguous()) + residual.float()
+            zb = z.to(residual.dtype)
+            zf = zb.float()
+            y = zf * torch.rsqrt(zf.pow(2).mean(-1, keepdim=True) + eps) * gamma.float()
+            residual_out.copy_(zb)
+            out.copy_(y.to(out.dtype))
+            return out, residual_out
+        self._comm.ar_rmsnorm(x, residual, gamma, out, residual_out, float(eps), sel.variant_id(variant), int(ctas))
+        return out, residual_out
+
     def _nccl(self, inp: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         if self.nccl_group is None:
             raise RuntimeError(

@@ -15,6 +15,7 @@
 
 #include "comm/communicator.h"
 #include "cpu/shm_comm.h"
+#include "fused/fused.h"
 #include "ops/ops.h"
 
 namespace py = pybind11;
@@ -128,6 +129,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   variants["copy"] = static_cast<int>(kCopy);
   m.attr("VARIANTS") = variants;
 
+  m.def("ar_rmsnorm_slot_bytes", &ar_rmsnorm_slot_bytes);
   m.def("workspace_bytes", &workspace_bytes, "bytes of one rank's workspace for a slot capacity");
   m.def("variant_slot_bytes", &variant_slot_bytes, "slot bytes a variant needs", py::arg("variant"),
         py::arg("bytes"), py::arg("world"));
@@ -209,6 +211,24 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
              return li.variant;
            },
            py::arg("inp"), py::arg("out"), py::arg("variant") = 0, py::arg("ctas") = 0)
+      .def("ar_rmsnorm",
+           [](Communicator& c, at::Tensor& x, at::Tensor& residual, at::Tensor& gamma, at::Tensor& y,
+              at::Tensor& residual_out, double eps, int variant, int ctas) {
+             for (const at::Tensor* t : {&x, &residual, &gamma, &y, &residual_out}) {
+               TORCH_CHECK(t->is_cuda() && t->is_contiguous() && t->scalar_type() == at::kBFloat16,
+                           "fused all-reduce + RMSNorm takes contiguous bf16 CUDA tensors");
+             }
+             const int64_t hidden = gamma.numel();
+             TORCH_CHECK(x.numel() % hidden == 0 && residual.numel() == x.numel() && y.numel() == x.numel() &&
+                             residual_out.numel() == x.numel(),
+                         "shape mismatch");
+             const at::cuda::OptionalCUDAGuard guard(device_of(x));
+             return ar_rmsnorm(c, at::cuda::getCurrentCUDAStream().stream(), x.data_ptr(), residual.data_ptr(),
+                               gamma.data_ptr(), y.data_ptr(), residual_out.data_ptr(), x.numel() / hidden, hidden,
+                               static_cast<float>(eps), variant, ctas);
+           },
+           py::arg("x"), py::arg("residual"), py::arg("gamma"), py::arg("y"), py::arg("residual_out"),
+           py::arg("eps"), py::arg("variant") = 0, py::arg("ctas") = 0)
       .def("check", &Communicator::check_status)
       .def("status",
            [](Communicator& c) {

@@ -1,0 +1,299 @@
+// Fused all-reduce + residual add + RMSNorm for tensor-parallel decode (sm_100a).
+//
+//   z = sum_ranks(x) + residual        (fp32 accumulation, rank order, rounded once)
+//   y = z * rsqrt(mean(z^2) + eps) * gamma
+//
+// Outputs: y and the new residual z (may alias the residual input). The
+// reference has no fused op (its kernels only sum, pcie_allreduce.cu:171-276);
+// this is the "all-reduce fused with residual-add + RMSNorm" path of the
+// BASELINE configuration, built on the same signal/slot protocol as the plain
+// all-reduce (generation counter, per-CTA bounded barriers, double-buffered slots).
+//
+// One CTA owns whole rows: a row of H bf16 values is H/8 16-byte packets and
+// every thread holds PPT packets of it in registers across the row reduction.
+//  * oneshot: every rank pushes its partial rows into slot[rank] of every peer,
+//    one barrier, then each rank reduces all rows locally (latency optimal).
+//  * twoshot: rows are split into N parts; rank p reduces and normalises part p,
+//    then every rank pulls the finished y and z rows of the other parts
+//    (2(N-1)/N of the bytes of one-shot's (N-1)).
+#include <algorithm>
+#include <stdexcept>
+
+#include "../comm/ar_kernels.cuh"
+#include "../comm/communicator.h"
+#include "fused.h"
+
+namespace b200ar {
+
+namespace {
+
+constexpr int kMaxRowThreads = 512;
+
+struct NormArgs {
+  CommCtx ctx;
+  char* slot[2][kMaxRanks];
+  const char* x;      // [T, H] partial sums of this rank
+  const char* res;    // [T, H] residual in
+  const char* gamma;  // [H]
+  char* y;            // [T, H] normalised output
+  char* z;            // [T, H] new residual (may alias res)
+  int rows;           // T
+  int hp;             // H / 8 packets per row
+  float eps;
+  float inv_h;
+};
+
+// Sum over the CTA; every thread gets the result.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();  // red[] may still be read from the previous row
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float t = lane < nw ? red[lane] : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  return t;
+}
+
+// Reduces row `row` from `n` copies (copy q at src + q * stride), adds the
+// residual, rounds z to bf16, normalises and stores y and z to the given
+// destinations (y2/z2 optional second destinations, e.g. an outbox).
+template <int N, int PPT>
+__device__ __forceinline__ void reduce_norm_row(const NormArgs& a, const char* src, int64_t stride_bytes,
+                                                int64_t row, char* ydst, char* zdst, char* y2, char* z2,
+                                                float* red) {
+  float zf[PPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < PPT; ++k) {
+    const int idx = threadIdx.x + k * blockDim.x;
+    if (idx < a.hp) {
+      uint4 v[N];
+#pragma unroll
+      for (int q = 0; q < N; ++q) v[q] = ld_cg(src + q * stride_bytes + static_cast<int64_t>(idx) * 16);
+      float acc[8];
+      unpack_set<__nv_bfloat16>(v[0], acc);
+#pragma unroll
+      for (int q = 1; q < N; ++q) unpack_add<__nv_bfloat16>(v[q], acc);
+      unpack_add<__nv_bfloat16>(ld_in(a.res + (row * a.hp + idx) * 16), acc);
+      const uint4 zp = pack<__nv_bfloat16>(acc);
+      st_out(zdst + (row * a.hp + idx) * 16, zp);
+      if (z2) st_cg(z2 + static_cast<int64_t>(idx) * 16, zp);
+      unpack_set<__nv_bfloat16>(zp, zf[k]);  // statistics of the stored (rounded) residual
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += zf[k][e] * zf[k][e];
+    }
+  }
+  const float inv = rsqrtf(block_sum(ss, red) * a.inv_h + a.eps);
+#pragma unroll
+  for (int k = 0; k < PPT; ++k) {
+    const int idx = threadIdx.x + k * blockDim.x;
+    if (idx < a.hp) {
+      float g[8];
+      unpack_set<__nv_bfloat16>(ld_in(a.gamma + static_cast<int64_t>(idx) * 16), g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) zf[k][e] = zf[k][e] * inv * g[e];
+      const uint4 yp = pack<__nv_bfloat16>(zf[k]);
+      st_out(ydst + (row * a.hp + idx) * 16, yp);
+      if (y2) st_cg(y2 + static_cast<int64_t>(idx) * 16, yp);
+    }
+  }
+}
+
+template <int N, int PPT>
+__global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_oneshot_kernel(NormArgs a) {
+  __shared__ uint32_t s_gen;
+  __shared__ float red[32];
+  const uint32_t gen = read_generation(a.ctx, &s_gen);
+  const int slot = gen & 1u;
+  const int r = a.ctx.rank;
+  const int64_t row_bytes = static_cast<int64_t>(a.hp) * 16;
+  char* dst[N];
+  rotate_ptrs<N>(a.slot[slot], r, dst);
+  // Phase 1: push this CTA's rows into slot row block [r] of every rank.
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+      const int idx = threadIdx.x + k * blockDim.x;
+      if (idx < a.hp) {
+        const uint4 v = ld_in(a.x + (row * a.hp + idx) * 16);
+        const int64_t off = (static_cast<int64_t>(r) * a.rows + row) * row_bytes + static_cast<int64_t>(idx) * 16;
+#pragma unroll
+        for (int p = 0; p < N; ++p) st_cg(dst[p] + off, v);
+      }
+    }
+  }
+  if (cta_barrier<N>(a.ctx, blockIdx.x, epoch_of(gen, 0))) {
+    const char* mine = a.slot[slot][r];
+    const int64_t stride = static_cast<int64_t>(a.rows) * row_bytes;
+    for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x)
+      reduce_norm_row<N, PPT>(a, mine + row * row_bytes, stride, row, a.y, a.z, nullptr, nullptr, red);
+  }
+  finish_generation(a.ctx, gen);
+}
+
+// Two-shot. Part p = rows [part_begin(T, N, p), part_begin(T, N, p + 1)); with
+// prow = ceil(T / N) rows per part, every slot holds
+//   inbox  [N][prow] rows : rank q's partial rows of this rank's part
+//   outbox [2][prow] rows : finished y rows, then z rows of this rank's part
+template <int N, int PPT>
+__global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_twoshot_kernel(NormArgs a) {
+  __shared__ uint32_t s_gen;
+  __shared__ float red[32];
+  const uint32_t gen = read_generation(a.ctx, &s_gen);
+  const int slot = gen & 1u;
+  const int r = a.ctx.rank;
+  const int64_t row_bytes = static_cast<int64_t>(a.hp) * 16;
+  const int prow = (a.rows + N - 1) / N;
+  char* peer[N];
+  rotate_ptrs<N>(a.slot[slot], r, peer);
+
+  // Phase 1: scatter partial rows of part p (k-th peer) to p's inbox row block r.
+#pragma unroll 1
+  for (int k = 0; k < N; ++k) {
+    const int p = (r + k) % N;
+    const int b = static_cast<int>(part_begin(a.rows, N, p));
+    const int e = static_cast<int>(part_begin(a.rows, N, p + 1));
+    for (int row = b + blockIdx.x; row < e; row += gridDim.x) {
+      char* dst = peer[k] + (static_cast<int64_t>(r) * prow + (row - b)) * row_bytes;
+#pragma unroll
+      for (int kk = 0; kk < PPT; ++kk) {
+        const int idx = threadIdx.x + kk * blockDim.x;
+        if (idx < a.hp) st_cg(dst + static_cast<int64_t>(idx) * 16, ld_in(a.x + (row * static_cast<int64_t>(a.hp) + idx) * 16));
+      }
+    }
+  }
+  bool ok = cta_barrier<N>(a.ctx, blockIdx.x, epoch_of(gen, 0));
+
+  // Phase 2: reduce + residual + norm of own part; results to outputs and outbox.
+  const int64_t outbox = static_cast<int64_t>(N) * prow * row_bytes;
+  if (ok) {
+    char* mine = peer[0];
+    const int b = static_cast<int>(part_begin(a.rows, N, r));
+    const int e = static_cast<int>(part_begin(a.rows, N, r + 1));
+    for (int row = b + blockIdx.x; row < e; row += gridDim.x) {
+      const int64_t lr = row - b;
+      reduce_norm_row<N, PPT>(a, mine + lr * row_bytes, static_cast<int64_t>(prow) * row_bytes, row, a.y, a.z,
+                              mine + outbox + lr * row_bytes, mine + outbox + (prow + lr) * row_bytes, red);
+    }
+  }
+  ok = cta_barrier<N>(a.ctx, blockIdx.x, epoch_of(gen, 1)) && ok;
+
+  // Phase 3: pull finished rows of the other parts.
+  if (ok) {
+#pragma unroll 1
+    for (int k = 1; k < N; ++k) {
+      const int p = (r + k) % N;
+      const int b = static_cast<int>(part_begin(a.rows, N, p));
+      const int e = static_cast<int>(part_begin(a.rows, N, p + 1));
+      for (int row = b + blockIdx.x; row < e; row += gridDim.x) {
+        const char* ysrc = peer[k] + outbox + static_cast<int64_t>(row - b) * row_bytes;
+        const char* zsrc = peer[k] + outbox + static_cast<int64_t>(prow + row - b) * row_bytes;
+#pragma unroll
+        for (int kk = 0; kk < PPT; ++kk) {
+          const int idx = threadIdx.x + kk * blockDim.x;
+          if (idx < a.hp) {
+            const uint4 yv = ld_cg(ysrc + static_cast<int64_t>(idx) * 16);
+            const uint4 zv = ld_cg(zsrc + static_cast<int64_t>(idx) * 16);
+            st_out(a.y + (row * static_cast<int64_t>(a.hp) + idx) * 16, yv);
+            st_out(a.z + (row * static_cast<int64_t>(a.hp) + idx) * 16, zv);
+          }
+        }
+      }
+    }
+  }
+  finish_generation(a.ctx, gen);
+}
+
+template <int N, int PPT>
+void launch_n(bool twoshot, int ctas, int threads, const NormArgs& a, cudaStream_t s) {
+  if (twoshot)
+    ar_rmsnorm_twoshot_kernel<N, PPT><<<ctas, threads, 0, s>>>(a);
+  else
+    ar_rmsnorm_oneshot_kernel<N, PPT><<<ctas, threads, 0, s>>>(a);
+}
+
+template <int PPT>
+void launch_ppt(int world, bool twoshot, int ctas, int threads, const NormArgs& a, cudaStream_t s) {
+  switch (world) {
+    case 1: launch_n<1, PPT>(twoshot, ctas, threads, a, s); break;
+    case 2: launch_n<2, PPT>(twoshot, ctas, threads, a, s); break;
+    case 3: launch_n<3, PPT>(twoshot, ctas, threads, a, s); break;
+    case 4: launch_n<4, PPT>(twoshot, ctas, threads, a, s); break;
+    case 5: launch_n<5, PPT>(twoshot, ctas, threads, a, s); break;
+    case 6: launch_n<6, PPT>(twoshot, ctas, threads, a, s); break;
+    case 7: launch_n<7, PPT>(twoshot, ctas, threads, a, s); break;
+    case 8: launch_n<8, PPT>(twoshot, ctas, threads, a, s); break;
+    default: throw std::invalid_argument("unsupported world size");
+  }
+}
+
+}  // namespace
+
+int64_t ar_rmsnorm_slot_bytes(int variant, int64_t rows, int64_t hidden, int world) {
+  const int64_t row_bytes = hidden * 2;
+  if (variant == kOneshotPush) return world * rows * row_bytes;
+  const int64_t prow = (rows + world - 1) / world;
+  return (world + 2) * prow * row_bytes;
+}
+
+int ar_rmsnorm(Communicator& comm, cudaStream_t stream, const void* x, const void* residual, const void* gamma,
+               void* y, void* residual_out, int64_t rows, int64_t hidden, float eps, int variant, int ctas) {
+  comm.check_status();
+  B200AR_CHECK(hidden % 8 == 0 && hidden / 8 <= 4 * kMaxRowThreads,
+               "hidden size must be a multiple of 8 and at most " << 32 * kMaxRowThreads);
+  B200AR_CHECK(rows >= 1 && rows < (1 << 30), "bad row count " << rows);
+  for (const void* p : {x, residual, gamma, static_cast<const void*>(y), static_cast<const void*>(residual_out)})
+    B200AR_CHECK(reinterpret_cast<uintptr_t>(p) % 16 == 0, "fused all-reduce + RMSNorm needs 16-byte aligned tensors");
+  const int world = comm.world();
+  if (variant == kAuto) {
+    // One-shot moves (N-1) rows per row and needs no second barrier; two-shot
+    // moves 2(N-1)/N and wins once the message is bandwidth bound.
+    const int64_t bytes = rows * hidden * 2;
+    variant = (world <= 2 || bytes <= (512 << 10) || rows < 2 * world) ? kOneshotPush : kTwoshot;
+  }
+  B200AR_CHECK(variant == kOneshotPush || variant == kTwoshot, "fused RMSNorm supports oneshot_push and twoshot");
+  if (world == 1) variant = kOneshotPush;
+  B200AR_CHECK(comm.slots_registered(), "communicator has no slot buffers");
+  const int64_t need = ar_rmsnorm_slot_bytes(variant, rows, hidden, world);
+  if (need > comm.slot_capacity()) {
+    const int other = variant == kTwoshot ? kOneshotPush : kTwoshot;
+    B200AR_CHECK(ar_rmsnorm_slot_bytes(other, rows, hidden, world) <= comm.slot_capacity(),
+                 "fused all-reduce + RMSNorm of " << rows << "x" << hidden << " needs " << need
+                                                  << " slot bytes, capacity is " << comm.slot_capacity());
+    variant = other;
+  }
+
+  NormArgs a{};
+  comm.fill_ctx(&a.ctx);
+  for (int s = 0; s < 2; ++s)
+    for (int i = 0; i < world; ++i) a.slot[s][i] = comm.slot_ptr(s, i);
+  a.x = static_cast<const char*>(x);
+  a.res = static_cast<const char*>(residual);
+  a.gamma = static_cast<const char*>(gamma);
+  a.y = static_cast<char*>(y);
+  a.z = static_cast<char*>(residual_out);
+  a.rows = static_cast<int>(rows);
+  a.hp = static_cast<int>(hidden / 8);
+  a.eps = eps;
+  a.inv_h = 1.0f / static_cast<float>(hidden);
+  const int ppt = a.hp <= kMaxRowThreads ? 1 : (a.hp <= 2 * kMaxRowThreads ? 2 : 4);
+  const int threads = std::max(32, ((a.hp + ppt - 1) / ppt + 31) / 32 * 32);
+  const bool two = variant == kTwoshot;
+  const int64_t work_rows = two ? (rows + world - 1) / world : rows;
+  int grid = ctas > 0 ? ctas : static_cast<int>(std::min<int64_t>(work_rows, 148));
+  grid = std::max(1, std::min(grid, kMaxCTAs));
+  switch (ppt) {
+    case 1: launch_ppt<1>(world, two, grid, threads, a, stream); break;
+    case 2: launch_ppt<2>(world, two, grid, threads, a, stream); break;
+    default: launch_ppt<4>(world, two, grid, threads, a, stream); break;
+  }
+  B200AR_CUDA(cudaGetLastError());
+  comm.count_launch();
+  return variant;
+}
+
+}  // namespace b200ar

@@ -1,0 +1,21 @@
+// Fused tensor-parallel collectives built on the Communicator's slots/signals.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace b200ar {
+
+class Communicator;
+
+// Slot bytes the fused all-reduce + RMSNorm needs for `rows` x `hidden` bf16.
+int64_t ar_rmsnorm_slot_bytes(int variant, int64_t rows, int64_t hidden, int world);
+
+// y = RMSNorm(sum_ranks(x) + residual) * gamma, residual_out = sum_ranks(x) + residual
+// (bf16 [rows, hidden]; residual_out may alias residual, y may alias x).
+// Returns the variant launched (kOneshotPush or kTwoshot).
+int ar_rmsnorm(Communicator& comm, cudaStream_t stream, const void* x, const void* residual, const void* gamma,
+               void* y, void* residual_out, int64_t rows, int64_t hidden, float eps, int variant, int ctas);
+
+}  // namespace b200ar

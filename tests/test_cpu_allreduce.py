@@ -138,3 +138,25 @@ def _world1(rank, world):
 
 def test_world_size_one():
     run_ranks(_world1, 1)
+
+
+def _fused_cpu(rank, world):
+    from b200ar import CustomAllreduce
+    from b200ar.ops.fused import ref_ar_residual_rmsnorm
+
+    comm = CustomAllreduce(device="cpu", max_size=1 << 20)
+    H = 1024
+    x = torch.randn(4, H, generator=torch.Generator().manual_seed(rank)).to(torch.bfloat16)
+    res = torch.randn(4, H, generator=torch.Generator().manual_seed(99)).to(torch.bfloat16)
+    gamma = torch.ones(H, dtype=torch.bfloat16)
+    xs = [None] * world
+    dist.all_gather_object(xs, x)
+    y_ref, z_ref = ref_ar_residual_rmsnorm(xs, res, gamma)
+    y, z = comm.all_reduce_residual_rmsnorm(x, res, gamma)
+    assert torch.equal(z, z_ref)
+    torch.testing.assert_close(y.float(), y_ref.float(), atol=2e-2, rtol=1e-2)
+    comm.close()
+
+
+def test_fused_residual_rmsnorm_cpu():
+    run_ranks(_fused_cpu, 2)

@@ -203,3 +203,38 @@ def _stress(rank, world):
 
 def test_stress_mixed_sizes():
     run_ranks(_stress, WORLD, backend="nccl")
+
+
+def _fused_rmsnorm(rank, world):
+    # BASELINE config 3 shapes: partial [T, 8192] ~ N(0,1), residual ~ N(0,1),
+    # gamma = 1 + 0.01 N(0,1), eps 1e-5, T in {1, 8, 32, 128, 512}.
+    from b200ar.ops.fused import ref_ar_residual_rmsnorm
+
+    comm = _comm(rank, max_size=32 << 20)
+    H = 8192
+    g0 = torch.Generator(device="cuda").manual_seed(7)
+    gamma = (1 + 0.01 * torch.randn(H, generator=g0, device="cuda")).to(torch.bfloat16)
+    for T in (1, 8, 32, 128, 512):
+        g = torch.Generator(device="cuda").manual_seed(1234 + rank + 17 * T)
+        x = torch.randn(T, H, generator=g, device="cuda").to(torch.bfloat16)
+        res = torch.randn(T, H, generator=torch.Generator(device="cuda").manual_seed(55 + T),
+                          device="cuda").to(torch.bfloat16)
+        xs = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(xs, x)
+        y_ref, z_ref = ref_ar_residual_rmsnorm(xs, res, gamma, 1e-5)
+        for variant in ("oneshot_push", "twoshot", "auto"):
+            y, z = comm.all_reduce_residual_rmsnorm(x, res, gamma, 1e-5, variant=variant)
+            torch.cuda.synchronize()
+            assert torch.equal(z, z_ref), (T, variant)
+            torch.testing.assert_close(y.float(), y_ref.float(), atol=2e-2, rtol=1e-2)
+        # In-place residual update.
+        r2 = res.clone()
+        y, z = comm.all_reduce_residual_rmsnorm(x, r2, gamma, 1e-5, residual_out=r2)
+        torch.cuda.synchronize()
+        assert z.data_ptr() == r2.data_ptr() and torch.equal(r2, z_ref)
+    comm.check()
+    comm.close()
+
+
+def test_fused_allreduce_residual_rmsnorm():
+    run_ranks(_fused_rmsnorm, WORLD, backend="nccl")

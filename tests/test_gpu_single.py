@@ -90,3 +90,26 @@ def test_world_one_copy_and_launch_count():
     assert comm.launches == n0 + 1
     comm.close()
     dist.destroy_process_group()
+
+
+def test_fused_rmsnorm_world_one():
+    import torch.distributed as dist
+
+    from dist_util import free_port
+
+    from b200ar import CustomAllreduce
+    from b200ar.ops.fused import ref_ar_residual_rmsnorm
+
+    if not dist.is_initialized():
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{free_port()}", rank=0, world_size=1)
+    comm = CustomAllreduce(device=torch.device("cuda", 0), max_size=8 << 20)
+    for H in (4096, 8192, 16384):
+        x = torch.randn(33, H, device="cuda").to(torch.bfloat16)
+        res = torch.randn(33, H, device="cuda").to(torch.bfloat16)
+        gamma = (1 + 0.01 * torch.randn(H, device="cuda")).to(torch.bfloat16)
+        y, z = comm.all_reduce_residual_rmsnorm(x, res, gamma, 1e-5)
+        y_ref, z_ref = ref_ar_residual_rmsnorm([x], res, gamma, 1e-5)
+        assert torch.equal(z, z_ref)
+        torch.testing.assert_close(y.float(), y_ref.float(), atol=2e-2, rtol=1e-2)
+    comm.close()
+    dist.destroy_process_group()
