@@ -39,17 +39,21 @@ class ClockSampler:
             cmd = [exe, f"--query-gpu={','.join(_FIELDS)}", "--format=csv,noheader,nounits", f"-lms={self.interval_ms}"]
             if self.gpus:
                 cmd.append(f"--id={self.gpus}")
-            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+                                         bufsize=1)
+            # Wait for the first sample so the timed region is covered from its start.
+            self.first = self.proc.stdout.readline()
         return self
 
     def __exit__(self, *exc):
         if self.proc is not None:
             self.proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
+                rest, _ = self.proc.communicate(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                self.out, _ = self.proc.communicate()
+                rest, _ = self.proc.communicate()
+            self.out = getattr(self, "first", "") + (rest or "")
         return False
 
     def summary(self) -> dict:

@@ -19,29 +19,42 @@ L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2 of B200
 
 
 class L2Flusher:
-    """Overwrites a buffer larger than L2 so the next kernel starts cold."""
+    """Overwrites a buffer larger than L2 so the next kernel starts cold.
 
-    def __init__(self, device, nbytes: int = L2_FLUSH_BYTES):
+    ``lead_us`` first keeps the GPU busy with a spin kernel so that the host
+    has enqueued the timed call (and its events) before the GPU reaches it;
+    otherwise a short kernel's event time would include host launch overhead.
+    """
+
+    def __init__(self, device, nbytes: int = L2_FLUSH_BYTES, lead_us: float = 60.0, sm_mhz: float = 1965.0):
         self.buf = torch.empty(nbytes // 4, dtype=torch.int32, device=device)
+        self.cycles = int(lead_us * sm_mhz)
 
     def __call__(self) -> None:
+        if self.cycles:
+            torch.cuda._sleep(self.cycles)
         self.buf.fill_(0x5A5A5A5A)
 
 
 class EventTimer:
     """Collects (start, end) CUDA event pairs keyed by name; ``times_ms`` syncs
-    once and returns every recorded duration."""
+    once and returns every recorded duration. Events come from a pool created
+    up front so that recording costs the host as little as possible."""
 
-    def __init__(self):
+    def __init__(self, pool: int = 0):
         self.pairs: Dict[str, List] = {}
+        self._pool = [torch.cuda.Event(enable_timing=True) for _ in range(pool)]
+
+    def _event(self):
+        return self._pool.pop() if self._pool else torch.cuda.Event(enable_timing=True)
 
     def start(self, key: str):
-        e = torch.cuda.Event(enable_timing=True)
+        e = self._event()
         e.record()
         self.pairs.setdefault(key, []).append([e, None])
 
     def stop(self, key: str):
-        e = torch.cuda.Event(enable_timing=True)
+        e = self._event()
         e.record()
         self.pairs[key][-1][1] = e
 

@@ -274,7 +274,8 @@ def run(args):
     torch.cuda.synchronize()
 
     # ---- timed region: exactly K steps, barrier + synchronize on both sides ----
-    timer = EventTimer()
+    n_keys = len(sz_list) * (1 + bool(graphs)) * (1 + with_nccl)
+    timer = EventTimer(pool=2 * n_keys * args.steps)
     dist.barrier()
     torch.cuda.synchronize()
     launches0 = arm.launches()
@@ -382,7 +383,15 @@ def run(args):
         if args.json_out:
             with open(args.json_out, "w") as f:
                 f.write(line + "\n")
-    dist.destroy_process_group()
+    # Graphs that captured NCCL calls can make process-group teardown hang, so
+    # drop them first and leave without destroying the NCCL communicator.
+    graphs.clear()
+    nccl_graphs.clear()
+    torch.cuda.synchronize()
+    dist.barrier(group=gloo)
+    sys.stdout.flush()
+    sys.stderr.flush()
+    os._exit(0)
 
 
 def main():
