@@ -30,8 +30,8 @@ class Config:
     variant: str = dataclasses.field(default_factory=lambda: os.environ.get("B200AR_VARIANT", "auto"))
     # Path of a measured selector table (JSON); empty = packaged default.
     selector_path: str = dataclasses.field(default_factory=lambda: os.environ.get("B200AR_SELECTOR", ""))
-    # Try NVLS (multimem) when the devices support multicast.
-    enable_nvls: bool = dataclasses.field(default_factory=lambda: os.environ.get("B200AR_NVLS", "1") != "0")
+    # Try NVLS (multimem) when the devices support multicast (opt-in: B200AR_NVLS=1).
+    enable_nvls: bool = dataclasses.field(default_factory=lambda: os.environ.get("B200AR_NVLS", "0") == "1")
     # Bytes of the device arena holding peer-pointer records for registered buffers.
     rank_data_bytes: int = dataclasses.field(default_factory=lambda: _env_int("B200AR_RANK_DATA_BYTES", 8 << 20))
 

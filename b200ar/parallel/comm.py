@@ -71,6 +71,8 @@ class CustomAllreduce:
             self._init_cpu()
         else:
             self._init_cuda()
+        if self.device.type == "cuda" and self.world > 1 and self.cfg.enable_nvls:
+            self._init_nvls()
         self.set_selector(sel.load_table(self.world, self.cfg.selector_path or None))
 
     # ------------------------------------------------------------------ setup
@@ -108,6 +110,28 @@ class CustomAllreduce:
             torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
         logger.info("rank %d: workspace %d bytes, slot capacity %d", self.rank, ws_bytes, self.slot_capacity)
+
+    def _init_nvls(self) -> None:
+        """Creates the NVLS multicast buffer (collective). Any failure on any
+        rank disables NVLS on every rank; the other variants stay available."""
+        from .nvls import register, setup_multicast
+
+        self.nvls = setup_multicast(self.group, self.rank, self.world, self.device, self.cfg.max_size)
+        if self.nvls is not None:
+            self._comm.set_nvls(self.nvls)
+            register(self)
+
+    def _release_nvls(self) -> None:
+        """Waits for this device, detaches and frees the multicast buffer."""
+        if self.nvls is None:
+            return
+        from .nvls import unregister
+
+        torch.cuda.synchronize(self.device)
+        if self._comm is not None:
+            self._comm.set_nvls(None)
+        self.nvls = None  # NvlsBuffer destructor unmaps, unbinds and releases
+        unregister(self)
 
     # -------------------------------------------------------------- selection
     def set_selector(self, entries) -> None:
@@ -245,6 +269,7 @@ class CustomAllreduce:
             torch.cuda.synchronize(self.device)
         if dist.is_initialized():
             dist.barrier(group=self.group)
+        self._release_nvls()
         if self._comm is not None:
             del self._comm
             self._comm = None

@@ -16,6 +16,7 @@
 #include "comm/communicator.h"
 #include "cpu/shm_comm.h"
 #include "fused/fused.h"
+#include "nvls/nvls.h"
 #include "ops/ops.h"
 
 namespace py = pybind11;
@@ -229,6 +230,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            },
            py::arg("x"), py::arg("residual"), py::arg("gamma"), py::arg("y"), py::arg("residual_out"),
            py::arg("eps"), py::arg("variant") = 0, py::arg("ctas") = 0)
+      // The caller keeps `buf` alive and detaches it (set_nvls(None)) before dropping it.
+      .def("set_nvls", [](Communicator& c, NvlsBuffer* b) { c.set_nvls(b); }, py::arg("buf").none(true))
+      .def_property_readonly("has_nvls", &Communicator::has_nvls)
       .def("check", &Communicator::check_status)
       .def("status",
            [](Communicator& c) {
@@ -244,6 +248,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
              return d;
            })
       .def("reset", [](Communicator& c) { c.reset(at::cuda::getCurrentCUDAStream().stream()); });
+
+  // ---- NVLS multicast buffers ----
+  py::class_<NvlsBuffer>(m, "NvlsBuffer")
+      .def(py::init<int, int, int64_t>(), py::arg("device"), py::arg("world"), py::arg("bytes"))
+      .def_static("supported", &NvlsBuffer::supported)
+      .def_property_readonly("bytes", &NvlsBuffer::bytes)
+      .def("create_and_export", &NvlsBuffer::create_and_export)
+      .def("import_handle", &NvlsBuffer::import_handle)
+      .def("add_device", &NvlsBuffer::add_device)
+      .def("bind_and_map", &NvlsBuffer::bind_and_map);
 
   // ---- CPU shared-memory backend ----
   py::class_<ShmComm>(m, "ShmComm")

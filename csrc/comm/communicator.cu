@@ -7,6 +7,7 @@
 
 #include "ar_kernels.cuh"
 #include "communicator.h"
+#include "../nvls/nvls.h"
 
 namespace b200ar {
 
@@ -246,6 +247,7 @@ LaunchInfo Communicator::plan(int64_t bytes, int variant, int ctas, bool capturi
           break;
         }
       }
+      if (v == kNvls && (nvls_ == nullptr || bytes > nvls_->bytes())) v = kTwoshot;
       // Fall back to the least demanding variant whose slot requirement fits.
       if (v == kOneshotPush || v == kOneshotPull || v == kTwoshot) {
         if (variant_slot_bytes(v, bytes, world_) > slot_cap_) {
@@ -262,7 +264,7 @@ LaunchInfo Communicator::plan(int64_t bytes, int variant, int ctas, bool capturi
     const int64_t packets = bytes / 16;
     const int64_t want = (packets + 2 * kArThreads - 1) / (2 * kArThreads);
     li.ctas = c > 0 ? c : static_cast<int>(std::clamp<int64_t>(want, 1, 148));
-  } else if (v == kTwoshot) {
+  } else if (v == kTwoshot || v == kNvls) {
     const int64_t part = bytes / 16 / world_;
     const int64_t want = (part + kArThreads - 1) / kArThreads;
     li.ctas = c > 0 ? c : static_cast<int>(std::clamp<int64_t>(want, 1, 2 * 148));
@@ -300,7 +302,11 @@ LaunchInfo Communicator::allreduce(cudaStream_t stream, const void* in, void* ou
     }
     return li;
   }
-  B200AR_CHECK(li.variant != kNvls, "NVLS all-reduce is served by the NVLS communicator");
+  if (li.variant == kNvls) {
+    B200AR_CHECK(nvls_ != nullptr, "variant nvls requested but no NVLS buffer is attached");
+    nvls_allreduce(*this, *nvls_, stream, in, out, bytes, static_cast<int>(dt), li.ctas);
+    return li;
+  }
   if (li.variant != kRegistered) {
     B200AR_CHECK(slots_ok_, "variant " << li.variant << " needs registered slot buffers");
     B200AR_CHECK(variant_slot_bytes(li.variant, bytes, world_) <= slot_cap_,

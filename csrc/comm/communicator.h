@@ -58,6 +58,7 @@ std::pair<void*, int64_t> allocation_range(const void* p);
 
 struct RankData;
 struct CommCtx;
+class NvlsBuffer;
 
 // One entry of the size-based selector: messages of at most `max_bytes` use
 // `variant` with `ctas` CTAs (0 = derive from size).
@@ -106,6 +107,12 @@ class Communicator {
   void register_graph_buffers(const std::vector<std::string>& handles,
                               const std::vector<std::vector<int64_t>>& offsets);
   int64_t pending_graph_buffers() const { return static_cast<int64_t>(graph_pending_.size()); }
+
+  // --- NVLS ---------------------------------------------------------------------
+  // Attaches a mapped multicast buffer (not owned); variant kNvls then runs the
+  // switch-reduction kernel for messages that fit it.
+  void set_nvls(NvlsBuffer* b) { nvls_ = b; }
+  bool has_nvls() const { return nvls_ != nullptr; }
 
   // --- configuration -------------------------------------------------------
   void set_timeout_ns(uint64_t ns) { timeout_ns_ = ns; }
@@ -164,6 +171,7 @@ class Communicator {
   uint64_t timeout_ns_ = 2000000000ull;
   std::vector<SelectorEntry> selector_;
   uint64_t launches_ = 0;
+  NvlsBuffer* nvls_ = nullptr;
 
  public:
   // Counts a kernel launched on behalf of this communicator (fused ops too).
