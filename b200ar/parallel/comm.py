@@ -91,7 +91,8 @@ class CustomAllreduce:
     def _init_cuda(self) -> None:
         self._shm = None
         with torch.cuda.device(self.device):
-            ws_bytes = _C.workspace_bytes(self.slot_capacity)
+            self.lamport_capacity = (min(self.cfg.lamport_max_size, self.cfg.max_size) + 15) // 16 * 16
+            ws_bytes = _C.workspace_bytes(self.slot_capacity) + _C.lamport_bytes(self.lamport_capacity, self.world)
             self._ws_ptr = _C.ipc_malloc(ws_bytes)
             handle = _C.ipc_get_handle(self._ws_ptr)
             handles: List[Optional[bytes]] = [None] * self.world
@@ -106,6 +107,9 @@ class CustomAllreduce:
             self._comm.register_slots(
                 [p + sig for p in ptrs], [p + sig + self.slot_capacity for p in ptrs], self.slot_capacity
             )
+            if self.world > 1 and self.lamport_capacity > 0:
+                lam = _C.workspace_bytes(self.slot_capacity)
+                self._comm.register_lamport([p + lam for p in ptrs], self.lamport_capacity)
             self._comm.set_timeout_ns(int(self.cfg.timeout_ms) * 1_000_000)
             torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)

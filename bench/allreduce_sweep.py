@@ -36,6 +36,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--tune", default="")
     ap.add_argument("--out", default="")
+    ap.add_argument("--nvls", action="store_true")
     args = ap.parse_args()
 
     rank = int(os.environ["RANK"])
@@ -46,7 +47,8 @@ def main():
     gloo = dist.new_group(backend="gloo")
     dev = torch.device("cuda", local)
     comm = CustomAllreduce(group=gloo, device=dev, nccl_group=dist.group.WORLD, max_size=args.max_bytes,
-                           push_max_size=max(1 << 20, args.max_bytes // 16))
+                           push_max_size=max(1 << 20, args.max_bytes // 16), lamport_max_size=4 << 20,
+                           enable_nvls=args.nvls)
     flush = L2Flusher(dev)
 
     sizes = []
@@ -61,10 +63,14 @@ def main():
         y = torch.empty_like(x)
         packets = s // 16
         cands = []
-        for v in ("oneshot_push", "oneshot_pull", "twoshot"):
-            if _C_slot(v, s, world) > comm.slot_capacity:
+        for v in ("oneshot_push", "oneshot_pull", "twoshot", "lamport", "nvls"):
+            if v in ("oneshot_push", "oneshot_pull", "twoshot") and _C_slot(v, s, world) > comm.slot_capacity:
                 continue
-            per = packets // world if v == "twoshot" else packets
+            if v == "lamport" and s > comm.lamport_capacity:
+                continue
+            if v == "nvls" and (comm.nvls is None or s > comm.nvls.bytes):
+                continue
+            per = packets // world if v in ("twoshot", "nvls") else packets
             for ctas in sorted({1, 2, 4, 8, 16, 32, 64, 148, 296, 444}):
                 if ctas > 1 and per // ctas < 32:
                     continue
@@ -111,7 +117,7 @@ def main():
             tables[world] = table
             sel.save_tables(args.tune, tables, {"how": "bench/allreduce_sweep.py, p50 of max over ranks"})
         print(json.dumps({"world": world, "table": table, "crossover_bytes": out["crossover_bytes"]}))
-    comm.close()
+    comm.close()  # releases the NVLS buffer before the process ends
     torch.cuda.synchronize()
     dist.barrier(group=gloo)
     sys.stdout.flush()

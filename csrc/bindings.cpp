@@ -128,9 +128,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   variants["registered"] = static_cast<int>(kRegistered);
   variants["nccl"] = static_cast<int>(kNccl);
   variants["copy"] = static_cast<int>(kCopy);
+  variants["lamport"] = static_cast<int>(kLamport);
   m.attr("VARIANTS") = variants;
 
   m.def("ar_rmsnorm_slot_bytes", &ar_rmsnorm_slot_bytes);
+  m.def("lamport_bytes", &lamport_bytes);
   m.def("workspace_bytes", &workspace_bytes, "bytes of one rank's workspace for a slot capacity");
   m.def("variant_slot_bytes", &variant_slot_bytes, "slot bytes a variant needs", py::arg("variant"),
         py::arg("bytes"), py::arg("world"));
@@ -171,6 +173,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("register_slots", &Communicator::register_slots, py::arg("ptrs0"), py::arg("ptrs1"),
            py::arg("capacity"))
       .def("register_buffer", &Communicator::register_buffer)
+      .def("register_lamport", &Communicator::register_lamport, py::arg("ptrs"), py::arg("capacity"))
+      .def_property_readonly("lamport_capacity", &Communicator::lamport_capacity)
       .def("graph_buffer_meta",
            [](Communicator& c) {
              auto [h, off] = c.graph_buffer_meta();

@@ -20,6 +20,7 @@ void launch_typed(int variant, int ctas, int threads, const ArArgs& a, cudaStrea
     case kOneshotPull: oneshot_pull_kernel<T, N><<<ctas, threads, 0, s>>>(a); break;
     case kTwoshot: twoshot_kernel<T, N><<<ctas, threads, 0, s>>>(a); break;
     case kRegistered: registered_kernel<T, N><<<ctas, threads, 0, s>>>(a); break;
+    case kLamport: oneshot_lamport_kernel<T, N><<<ctas, threads, 0, s>>>(a); break;
     default: throw std::invalid_argument("unknown all-reduce variant " + std::to_string(variant));
   }
 }
@@ -47,6 +48,18 @@ __global__ void __launch_bounds__(kArThreads) copy_kernel(const char* __restrict
 }
 
 }  // namespace
+
+__global__ void fill_u32_kernel(uint32_t* p, int64_t words, uint32_t value) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < words;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    p[i] = value;
+}
+
+void launch_lamport_init(void* p, int64_t bytes, cudaStream_t stream) {
+  if (bytes <= 0) return;
+  fill_u32_kernel<<<256, 256, 0, stream>>>(static_cast<uint32_t*>(p), bytes / 4, kLamportMarker);
+  B200AR_CUDA(cudaGetLastError());
+}
 
 void launch_copy(const void* in, void* out, int64_t packets, cudaStream_t stream) {
   const int64_t want = std::max<int64_t>((packets + kArThreads - 1) / kArThreads, 1);

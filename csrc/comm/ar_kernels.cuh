@@ -37,6 +37,8 @@ struct ArArgs {
   char* out;                 // local output
   const RankData* rd;        // registered variant only
   int64_t packets;           // message size in 16-byte packets
+  char* lam[kMaxRanks];      // Lamport region of every rank (peer mappings)
+  int64_t lam_cap;           // bytes per (buffer, source) block of the Lamport region
 };
 
 // Fills d[k] = base[(rank + k) % N] without dynamic indexing of a local array.
@@ -236,12 +238,110 @@ __global__ void __launch_bounds__(kArThreads) registered_kernel(ArArgs a) {
   finish_generation(a.ctx, gen);
 }
 
+// ---------------------------------------------------------------------------
+// One-shot Lamport: no barrier and no fence. Every rank writes its packets
+// straight into the peers' current buffer; a receiver polls its own buffer
+// until no 32-bit word of a packet is the marker, sums in rank order, then
+// restores the marker so the buffer is ready for its next use.
+//
+// Buffer b = gen % 3 on rank r is [N sources][lam_cap bytes]. Reuse is safe:
+// a writer reaches the same buffer again only at gen + 3, after it consumed
+// this rank's data of gen + 1 and gen + 2, which this rank pushed after it had
+// restored the markers of gen (stream order).
+// ---------------------------------------------------------------------------
+
+B200AR_DEV uint4 ld_volatile16(const void* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+B200AR_DEV bool lamport_ready(const uint4& v) {
+  return v.x != kLamportMarker && v.y != kLamportMarker && v.z != kLamportMarker && v.w != kLamportMarker;
+}
+
+// Replaces -0.0 elements by +0.0 so that no word equals the marker.
+template <typename T>
+B200AR_DEV uint32_t lamport_clean(uint32_t w) {
+  if constexpr (sizeof(T) == 4) {
+    return w == kLamportMarker ? 0u : w;
+  } else {
+    if ((w & 0xffffu) == 0x8000u) w &= 0xffff0000u;
+    if ((w >> 16) == 0x8000u) w &= 0x0000ffffu;
+    return w;
+  }
+}
+
+template <typename T, int N>
+__global__ void __launch_bounds__(kArThreads) oneshot_lamport_kernel(ArArgs a) {
+  __shared__ uint32_t s_gen;
+  const uint32_t gen = read_generation(a.ctx, &s_gen);
+  const int r = a.ctx.rank;
+  const int64_t P = a.packets;
+  const int64_t b = part_begin(P, gridDim.x, blockIdx.x);
+  const int64_t e = part_begin(P, gridDim.x, blockIdx.x + 1);
+  const int64_t buf_off = static_cast<int64_t>(gen % kLamportBuffers) * N * a.lam_cap;
+
+  char* dst[N];
+  rotate_ptrs<N>(a.lam, r, dst);
+  const int64_t my_off = buf_off + static_cast<int64_t>(r) * a.lam_cap;
+  for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) {
+    uint4 v = ld_in(a.in + i * 16);
+    v.x = lamport_clean<T>(v.x);
+    v.y = lamport_clean<T>(v.y);
+    v.z = lamport_clean<T>(v.z);
+    v.w = lamport_clean<T>(v.w);
+#pragma unroll
+    for (int k = 0; k < N; ++k) st_cg(dst[k] + my_off + i * 16, v);
+  }
+
+  char* mine = a.lam[r] + buf_off;
+  const uint4 marker = make_uint4(kLamportMarker, kLamportMarker, kLamportMarker, kLamportMarker);
+  bool fail = false;
+  for (int64_t i = b + threadIdx.x; i < e && !fail; i += blockDim.x) {
+    uint4 v[N];
+#pragma unroll
+    for (int q = 0; q < N; ++q) v[q] = ld_volatile16(mine + q * a.lam_cap + i * 16);
+#pragma unroll
+    for (int q = 0; q < N; ++q) {
+      if (!lamport_ready(v[q]) && !fail) {
+        const uint64_t start = global_ns();
+        uint32_t spins = 0;
+        while (!lamport_ready(v[q] = ld_volatile16(mine + q * a.lam_cap + i * 16))) {
+          if ((++spins & 63u) == 0u && global_ns() - start > a.ctx.timeout_ns) {
+            report_status(a.ctx.status, kStatusTimeout, r, q, blockIdx.x, gen, 0);
+            fail = true;
+            break;
+          }
+        }
+      }
+    }
+    if (fail) break;
+    float acc[PackTraits<T>::kElems];
+    unpack_set<T>(v[0], acc);
+#pragma unroll
+    for (int q = 1; q < N; ++q) unpack_add<T>(v[q], acc);
+    st_out(a.out + i * 16, pack<T>(acc));
+#pragma unroll
+    for (int q = 0; q < N; ++q) st_cg(mine + q * a.lam_cap + i * 16, marker);
+  }
+  finish_generation(a.ctx, gen);
+}
+
+// Fills `words` 32-bit words at p with `value` (Lamport region initialisation).
+__global__ void fill_u32_kernel(uint32_t* p, int64_t words, uint32_t value);
+
 }  // namespace b200ar
 
 namespace b200ar {
 // Host launcher for the kernels above (ar_kernels.cu).
 void launch_ar_kernel(int variant, DType dt, int world, int ctas, int threads, const ArArgs& args,
                       cudaStream_t stream);
+// Fills a device range with the Lamport marker.
+void launch_lamport_init(void* p, int64_t bytes, cudaStream_t stream);
 // World size 1: out = in (16-byte packets) with a b200ar kernel.
 void launch_copy(const void* in, void* out, int64_t packets, cudaStream_t stream);
 }  // namespace b200ar

@@ -174,6 +174,18 @@ void Communicator::register_slots(const std::vector<int64_t>& ptrs0, const std::
   }
 }
 
+void Communicator::register_lamport(const std::vector<int64_t>& ptrs, int64_t cap) {
+  B200AR_CHECK(static_cast<int>(ptrs.size()) == world_, "need one Lamport region per rank");
+  B200AR_CHECK(cap > 0 && cap % 16 == 0, "Lamport capacity must be a positive multiple of 16");
+  for (int i = 0; i < world_; ++i) {
+    B200AR_CHECK(ptrs[i] % 16 == 0, "Lamport regions must be 16-byte aligned");
+    lam_[i] = reinterpret_cast<char*>(ptrs[i]);
+  }
+  lam_cap_ = cap;
+  launch_lamport_init(lam_[rank_], lamport_bytes(cap, world_), nullptr);
+  B200AR_CUDA(cudaDeviceSynchronize());
+}
+
 void Communicator::register_buffer(const std::vector<int64_t>& ptrs) {
   B200AR_CHECK(static_cast<int>(ptrs.size()) == world_, "need one buffer pointer per rank");
   RankData rd{};
@@ -248,6 +260,7 @@ LaunchInfo Communicator::plan(int64_t bytes, int variant, int ctas, bool capturi
         }
       }
       if (v == kNvls && (nvls_ == nullptr || bytes > nvls_->bytes())) v = kTwoshot;
+      if (v == kLamport && (lam_cap_ == 0 || bytes > lam_cap_)) v = kOneshotPush;
       // Fall back to the least demanding variant whose slot requirement fits.
       if (v == kOneshotPush || v == kOneshotPull || v == kTwoshot) {
         if (variant_slot_bytes(v, bytes, world_) > slot_cap_) {
@@ -260,7 +273,7 @@ LaunchInfo Communicator::plan(int64_t bytes, int variant, int ctas, bool capturi
     }
   }
   li.variant = v;
-  if (v == kOneshotPush || v == kOneshotPull || v == kRegistered) {
+  if (v == kOneshotPush || v == kOneshotPull || v == kRegistered || v == kLamport) {
     const int64_t packets = bytes / 16;
     const int64_t want = (packets + 2 * kArThreads - 1) / (2 * kArThreads);
     li.ctas = c > 0 ? c : static_cast<int>(std::clamp<int64_t>(want, 1, 148));
@@ -307,7 +320,10 @@ LaunchInfo Communicator::allreduce(cudaStream_t stream, const void* in, void* ou
     nvls_allreduce(*this, *nvls_, stream, in, out, bytes, static_cast<int>(dt), li.ctas);
     return li;
   }
-  if (li.variant != kRegistered) {
+  if (li.variant == kLamport) {
+    B200AR_CHECK(lam_cap_ > 0 && bytes <= lam_cap_, "message of " << bytes << " bytes exceeds the Lamport capacity "
+                                                                   << lam_cap_);
+  } else if (li.variant != kRegistered) {
     B200AR_CHECK(slots_ok_, "variant " << li.variant << " needs registered slot buffers");
     B200AR_CHECK(variant_slot_bytes(li.variant, bytes, world_) <= slot_cap_,
                  "message of " << bytes << " bytes needs " << variant_slot_bytes(li.variant, bytes, world_)
@@ -322,6 +338,8 @@ LaunchInfo Communicator::allreduce(cudaStream_t stream, const void* in, void* ou
   a.in = static_cast<const char*>(in);
   a.out = static_cast<char*>(out);
   a.packets = bytes / 16;
+  for (int i = 0; i < world_; ++i) a.lam[i] = lam_[i];
+  a.lam_cap = lam_cap_;
   if (li.variant == kRegistered) {
     if (capturing) {
       if (arena_next_ + graph_pending_.size() + 1 > arena_end_) throw std::runtime_error("Rank data buffer overflow");

@@ -98,6 +98,12 @@ class Communicator {
   // allocation size of this rank's buffers".
   void register_slots(const std::vector<int64_t>& ptrs0, const std::vector<int64_t>& ptrs1, int64_t capacity);
 
+  // Registers the Lamport regions (ptrs[i] = rank i's region of
+  // lamport_bytes(cap, world) bytes) and fills this rank's region with the
+  // marker. Every rank must finish this before any rank uses kLamport.
+  void register_lamport(const std::vector<int64_t>& ptrs, int64_t cap);
+  int64_t lamport_capacity() const { return lam_cap_; }
+
   // Registers a static user buffer: ptrs[i] = rank i's copy (already mapped).
   void register_buffer(const std::vector<int64_t>& ptrs);
 
@@ -172,6 +178,8 @@ class Communicator {
   std::vector<SelectorEntry> selector_;
   uint64_t launches_ = 0;
   NvlsBuffer* nvls_ = nullptr;
+  char* lam_[kMaxRanks] = {};
+  int64_t lam_cap_ = 0;
 
  public:
   // Counts a kernel launched on behalf of this communicator (fused ops too).

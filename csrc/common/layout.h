@@ -85,6 +85,7 @@ B200AR_HD int64_t part_begin(int64_t total, int parts, int i) { return (total * 
 // Workspace of one rank: [Signal][slot 0][slot 1]; `cap` bytes per slot.
 B200AR_HD int64_t signal_bytes() { return static_cast<int64_t>(sizeof(Signal)); }
 B200AR_HD int64_t workspace_bytes(int64_t cap) { return signal_bytes() + 2 * cap; }
+
 B200AR_HD int64_t slot_offset(int slot, int64_t cap) { return signal_bytes() + slot * cap; }
 
 // Algorithm variants. The integer values are part of the Python API.
@@ -97,7 +98,17 @@ enum Variant : int {
   kRegistered = 5,    // pull directly from registered peer buffers, start + end barrier
   kNccl = 6,          // fall back to NCCL (handled by the Python layer)
   kCopy = 7,          // world size 1: plain copy
+  kLamport = 8,       // push with in-band "not yet written" markers: no barrier, no fence
 };
+
+// The one-shot Lamport variant keeps kLamportBuffers rotating buffers of
+// world x lamport_cap bytes per rank, pre-filled with this 32-bit marker
+// (the bit pattern of -0.0f; for 16-bit types the word (+0, -0)). Writers turn
+// every -0.0 element into +0.0, so real data never contains the marker word.
+constexpr int kLamportBuffers = 3;
+constexpr uint32_t kLamportMarker = 0x80000000u;
+
+B200AR_HD int64_t lamport_bytes(int64_t lamport_cap, int world) { return kLamportBuffers * world * lamport_cap; }
 
 // Slot bytes a variant needs for a message of `bytes` bytes on `world` ranks.
 // Two-shot: world parts of ceil(packets / world) 16-byte packets for the

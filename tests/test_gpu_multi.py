@@ -16,7 +16,7 @@ if NGPU < 2:
     pytest.skip("needs at least two GPUs", allow_module_level=True)
 WORLD = min(NGPU, 8)
 
-VARIANTS = ["oneshot_push", "oneshot_pull", "twoshot"]
+VARIANTS = ["oneshot_push", "oneshot_pull", "twoshot", "lamport"]
 
 
 def _oracle(x, world):
@@ -48,6 +48,8 @@ def _variants_dtypes(rank, world):
                 nbytes = numel * x.element_size()
                 if variant == "oneshot_push" and nbytes * world > comm.slot_capacity:
                     continue
+                if variant == "lamport" and nbytes > comm.lamport_capacity:
+                    continue
                 for ctas in (0, 1, 7):
                     out = comm.all_reduce(x, variant=variant, ctas=ctas)
                     torch.cuda.synchronize()
@@ -76,7 +78,7 @@ def _graph_replay(rank, world):
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        for variant in ("oneshot_push", "twoshot", "oneshot_pull"):
+        for variant in ("oneshot_push", "twoshot", "oneshot_pull", "lamport"):
             comm.all_reduce(inp, mid, variant=variant)
             mid.mul_(1.0 / world)
             comm.all_reduce(mid, out, variant=variant)
@@ -190,7 +192,7 @@ def _stress(rank, world):
         n = sizes[int(torch.randint(len(sizes), (1,), generator=gen))]
         v = float(rank + 1) + (i % 11) * 0.125
         x = torch.full((n,), v, dtype=torch.float32, device="cuda")
-        out = comm.all_reduce(x)
+        out = comm.all_reduce(x, variant="lamport" if (i % 3 == 0 and n * 4 <= comm.lamport_capacity) else "auto")
         last = (out, sum(float(r + 1) + (i % 11) * 0.125 for r in range(world)))
         if i % 97 == 0:
             torch.cuda.synchronize()
@@ -238,3 +240,34 @@ def _fused_rmsnorm(rank, world):
 
 def test_fused_allreduce_residual_rmsnorm():
     run_ranks(_fused_rmsnorm, WORLD, backend="nccl")
+
+
+def _nvls(rank, world):
+    # NVLS is opt-in; the buffer is always released (a process that exits with
+    # memory bound to a multicast object can fault the peers).
+    comm = _comm(rank, max_size=64 << 20, enable_nvls=True)
+    try:
+        if comm.nvls is None:
+            return
+        for dtype in (torch.bfloat16, torch.float32):
+            for numel in (8 * 1024, 1 << 20, 16 << 20):
+                if numel * torch.tensor([], dtype=dtype).element_size() > (64 << 20):
+                    continue
+                g = torch.Generator(device="cuda").manual_seed(rank + numel)
+                x = (torch.rand(numel, generator=g, device="cuda") * 2 - 1).to(dtype)
+                ref = _oracle(x, world)
+                for _ in range(3):
+                    out = comm.all_reduce(x, variant="nvls")
+                    torch.cuda.synchronize()
+                    torch.testing.assert_close(out.float(), ref, atol=2e-2 * world, rtol=1e-2)
+                # Every rank receives the same multicast value.
+                outs = [torch.empty_like(out) for _ in range(world)]
+                dist.all_gather(outs, out)
+                assert all(torch.equal(o, outs[0]) for o in outs)
+        comm.check()
+    finally:
+        comm.close()
+
+
+def test_nvls_multimem():
+    run_ranks(_nvls, WORLD, backend="nccl")

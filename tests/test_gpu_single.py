@@ -45,11 +45,14 @@ def _local_comm(world, cap=1 << 20, timeout_ms=20):
     comm = C.Comm(ws, rank_data, 0)
     sig = C.SIGNAL_BYTES
     comm.register_slots([p + sig for p in ws], [p + sig + cap for p in ws], cap)
+    lam = [C.ipc_malloc(C.lamport_bytes(1 << 16, world)) for _ in range(world)]
+    comm.register_lamport(lam, 1 << 16)
+    ws = ws + lam
     comm.set_timeout_ns(timeout_ms * 1_000_000)
     return comm, ws, rank_data
 
 
-@pytest.mark.parametrize("variant", ["oneshot_push", "oneshot_pull", "twoshot"])
+@pytest.mark.parametrize("variant", ["oneshot_push", "oneshot_pull", "twoshot", "lamport"])
 def test_barrier_timeout_reports_status(variant):
     from b200ar import CommTimeoutError
     from b200ar.parallel.selector import VARIANTS
