@@ -1,0 +1,24 @@
+// Host API of the tcgen05 GEMM (gemm.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace b200ar {
+
+namespace gemm {
+struct Shape;
+}
+
+// 2-D bf16 tensor map (row-major [rows, cols], leading dimension ld elements)
+// with a box of box_rows x box_cols and 128-byte swizzle; no multicast.
+CUtensorMap make_tmap_bf16_2d(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows, int box_cols);
+
+// C[M, N] (bf16, row-major) = A[M, K] * B[N, K]^T. `err` is a device int that
+// receives a non-zero code if a bounded wait expired.
+void gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int* err,
+               cudaStream_t stream, int max_ctas = 0);
+
+}  // namespace b200ar

@@ -1,0 +1,42 @@
+"""tcgen05 GEMM against a PyTorch fp32 reference of the same op."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a GPU", allow_module_level=True)
+
+
+@pytest.mark.parametrize(
+    "m,n,k",
+    [(128, 256, 64), (16, 8192, 3584), (128, 8192, 3584), (1024, 8192, 3584), (1, 512, 128), (200, 264, 72),
+     (4096, 1024, 8192)],
+)
+def test_gemm_matches_fp32(m, n, k):
+    from b200ar.ops.gemm import check_errors, linear
+
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + n + k)
+    a = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+    w = (0.02 * torch.randn(n, k, generator=g, device="cuda")).to(torch.bfloat16)
+    out = linear(a, w)
+    torch.cuda.synchronize()
+    check_errors()
+    ref = a.float() @ w.float().t()
+    err = (out.float() - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    assert err <= 1e-2 * scale + 1e-2, (err, scale)
+
+
+def test_gemm_repeated_and_capped_grid():
+    from b200ar.ops.gemm import check_errors, linear
+
+    a = torch.randn(512, 1024, device="cuda").to(torch.bfloat16)
+    w = torch.randn(2048, 1024, device="cuda").to(torch.bfloat16)
+    ref = (a.float() @ w.float().t()).to(torch.bfloat16)
+    for ctas in (1, 3, 0):
+        out = linear(a, w, max_ctas=ctas)
+        torch.cuda.synchronize()
+        check_errors()
+        torch.testing.assert_close(out.float(), ref.float(), atol=0.5, rtol=2e-2)
