@@ -1,0 +1,73 @@
+"""tcgen05 GEMM throughput vs cuBLAS (torch.matmul) on the BASELINE config-4
+shapes (x [M, 3584] @ W[8192, 3584]^T, M in {16, 128, 1024, 8192}) plus a
+square 8192^3 case. CUDA-event timing, L2 flushed before every call, p50.
+
+    python bench/gemm_bench.py [--iters 50]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+from b200ar.ops.gemm import check_errors, linear  # noqa: E402
+from b200ar.utils.timing import EventTimer, L2Flusher, percentile  # noqa: E402
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--shapes", default="16x8192x3584,128x8192x3584,1024x8192x3584,8192x8192x3584,8192x8192x8192")
+    args = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    flush = L2Flusher(dev, lead_us=20)
+    peaks = {}
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        peaks = json.load(open(p))
+    rows = []
+    for shp in args.shapes.split(","):
+        m, n, k = (int(v) for v in shp.split("x"))
+        a = torch.randn(m, k, device=dev).to(torch.bfloat16)
+        w = (0.02 * torch.randn(n, k, device=dev)).to(torch.bfloat16)
+        out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+        timer = EventTimer(pool=4 * args.iters)
+        for it in range(args.warmup + args.iters):
+            for name in ("tcgen05", "cublas"):
+                flush()
+                if it >= args.warmup:
+                    timer.start(name)
+                if name == "tcgen05":
+                    linear(a, w, out=out)
+                else:
+                    torch.matmul(a, w.t(), out=out)
+                if it >= args.warmup:
+                    timer.stop(name)
+        t = timer.times_ms()
+        check_errors()
+        flops = 2.0 * m * n * k
+        row = {"M": m, "N": n, "K": k}
+        for name in ("tcgen05", "cublas"):
+            us = percentile(t[name], 50) * 1e3
+            row[f"{name}_us"] = round(us, 2)
+            row[f"{name}_tflops"] = round(flops / (us * 1e-6) / 1e12, 1)
+        if peaks.get("bf16_tflops"):
+            row["tcgen05_frac_of_measured_peak"] = round(row["tcgen05_tflops"] / peaks["bf16_tflops"], 3)
+        # Weight-streaming bound for small M: bytes of A, B and C over measured HBM bandwidth.
+        if peaks.get("hbm_gbs"):
+            bytes_ = 2 * (m * k + n * k + m * n)
+            row["hbm_bound_us"] = round(bytes_ / (peaks["hbm_gbs"] * 1e9) * 1e6, 2)
+        rows.append(row)
+        print(json.dumps(row), flush=True)
+
+
+if __name__ == "__main__":
+    main()
