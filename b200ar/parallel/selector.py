@@ -50,9 +50,11 @@ def load_table(world: int, path: Optional[str] = None) -> List[Entry]:
     if os.path.exists(p):
         with open(p) as f:
             data = json.load(f)
-        rows = data.get("tables", {}).get(str(world))
-        if rows:
-            return [(int(b), str(v), int(c)) for b, v, c in rows]
+        tables = {int(k): v for k, v in data.get("tables", {}).items() if v}
+        if tables:
+            # Nearest measured world size (ties go to the larger one).
+            best = min(tables, key=lambda w: (abs(w - world), -w))
+            return [(int(b), str(v), int(c)) for b, v, c in tables[best]]
     return list(FALLBACK)
 
 

@@ -94,8 +94,11 @@ class OursArm:
         sys.path.insert(0, ROOT)
         from b200ar import CustomAllreduce
 
+        # NVLS (switch reduction) pays off from 4 ranks up; its multicast
+        # buffer is released in close() before the process ends.
+
         self.comm = CustomAllreduce(group=gloo, device=torch.device("cuda", torch.cuda.current_device()),
-                                    nccl_group=dist.group.WORLD, max_size=max_bytes)
+                                    nccl_group=dist.group.WORLD, max_size=max_bytes, enable_nvls=world > 2)
 
     def all_reduce(self, inp, out):
         self.comm.all_reduce(inp, out)

@@ -37,6 +37,7 @@ def main():
     ap.add_argument("--tune", default="")
     ap.add_argument("--out", default="")
     ap.add_argument("--nvls", action="store_true")
+    ap.add_argument("--ctas", type=lambda v: [int(x) for x in v.split(",")], default=[1, 2, 4, 8, 16, 32, 64, 148, 296, 444])
     args = ap.parse_args()
 
     rank = int(os.environ["RANK"])
@@ -71,7 +72,7 @@ def main():
             if v == "nvls" and (comm.nvls is None or s > comm.nvls.bytes):
                 continue
             per = packets // world if v in ("twoshot", "nvls") else packets
-            for ctas in sorted({1, 2, 4, 8, 16, 32, 64, 148, 296, 444}):
+            for ctas in args.ctas:
                 if ctas > 1 and per // ctas < 32:
                     continue
                 if ctas > 512:

@@ -174,9 +174,9 @@ NvlsBuffer::NvlsBuffer(int device, int world, int64_t bytes) : device_(device), 
   B200AR_CHECK(world >= 2 && world <= kMaxRanks, "NVLS needs 2..8 ranks");
   size_t mc_gran = 0, mem_gran = 0;
   CUmulticastObjectProp mp = mc_prop(world, static_cast<size_t>(bytes));
-  CU(cuMulticastGetGranularity, &mc_gran, &mp, CU_MULTICAST_GRANULARITY_RECOMMENDED);
+  CU(cuMulticastGetGranularity, &mc_gran, &mp, CU_MULTICAST_GRANULARITY_MINIMUM);
   CUmemAllocationProp pp = phys_prop(device);
-  CU(cuMemGetAllocationGranularity, &mem_gran, &pp, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED);
+  CU(cuMemGetAllocationGranularity, &mem_gran, &pp, CU_MEM_ALLOC_GRANULARITY_MINIMUM);
   bytes_ = static_cast<int64_t>(round_up(round_up(static_cast<size_t>(bytes), mc_gran), mem_gran));
 }
 
