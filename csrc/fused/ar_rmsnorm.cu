@@ -297,3 +297,112 @@ int ar_rmsnorm(Communicator& comm, cudaStream_t stream, const void* x, const voi
 }
 
 }  // namespace b200ar
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point (declared in noalloc.h). It runs the one-shot
+// kernel above with world size 1; the signal block and both staging slots
+// live in a file-scope device array instead of memory the caller allocates.
+// ---------------------------------------------------------------------------
+
+#include <mutex>
+#include <string>
+
+#include "noalloc.h"
+
+namespace {
+
+constexpr int64_t kNoallocSlot = B200AR_NOALLOC_MAX_BYTES;
+constexpr int64_t kNoallocScratch = sizeof(b200ar::Signal) + 2 * kNoallocSlot;
+constexpr int kNoallocMaxDevices = 64;
+
+// Scratch for every GPU that loads this library: [Signal][slot 0][slot 1].
+// In host code this name is only a stand-in for the symbol; the device address
+// comes from cudaGetSymbolAddress.
+static __device__ __align__(256) char g_noalloc_scratch[kNoallocScratch];
+
+std::mutex g_noalloc_mu;
+char* g_noalloc_ptr[kNoallocMaxDevices] = {};
+thread_local std::string g_noalloc_err;
+
+int noalloc_fail(int code, const std::string& msg) {
+  g_noalloc_err = msg;
+  return code;
+}
+
+// Once per device, with that device current: device address of the scratch
+// array and a cleared signal block.
+int noalloc_setup(int dev, char** out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return noalloc_fail(3, std::string("cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+    e = cudaMemset(p, 0, sizeof(b200ar::Signal));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return noalloc_fail(3, std::string("clearing the scratch signal block failed: ") +
+                                                     cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<char*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
+}  // namespace
+
+extern "C" int b200ar_residual_rmsnorm_noalloc(const void* x, const void* residual, const void* gamma, void* y,
+                                               void* residual_out, int64_t rows, int64_t hidden, float eps,
+                                               cudaStream_t stream) {
+  using namespace b200ar;
+  if (rows < 1 || hidden < 8 || hidden % 8 != 0 || hidden > 16384)
+    return noalloc_fail(1, "hidden must be a multiple of 8 in [8, 16384] and rows >= 1");
+  if (rows * hidden * 2 > kNoallocSlot)
+    return noalloc_fail(1, "rows * hidden * 2 = " + std::to_string(rows * hidden * 2) +
+                               " bytes exceeds the allocation-free limit of " + std::to_string(kNoallocSlot) +
+                               " bytes");
+  for (const void* p : {x, residual, gamma, static_cast<const void*>(y), static_cast<const void*>(residual_out)})
+    if (p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 != 0)
+      return noalloc_fail(1, "all tensors must be non-null and 16-byte aligned");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kNoallocMaxDevices) return noalloc_fail(3, "no usable current device");
+  char* base = nullptr;
+  if (int rc = noalloc_setup(dev, &base)) return rc;
+
+  NormArgs a{};
+  a.ctx.self = reinterpret_cast<Signal*>(base);
+  a.ctx.peers[0] = a.ctx.self;
+  a.ctx.status = nullptr;  // one rank: the barrier never waits on another GPU
+  a.ctx.timeout_ns = 1000000000ull;
+  a.ctx.rank = 0;
+  a.ctx.world = 1;
+  a.slot[0][0] = base + sizeof(Signal);
+  a.slot[1][0] = base + sizeof(Signal) + kNoallocSlot;
+  a.x = static_cast<const char*>(x);
+  a.res = static_cast<const char*>(residual);
+  a.gamma = static_cast<const char*>(gamma);
+  a.y = static_cast<char*>(y);
+  a.z = static_cast<char*>(residual_out);
+  a.rows = static_cast<int>(rows);
+  a.hp = static_cast<int>(hidden / 8);
+  a.eps = eps;
+  a.inv_h = 1.0f / static_cast<float>(hidden);
+  const int ppt = a.hp <= kMaxRowThreads ? 1 : (a.hp <= 2 * kMaxRowThreads ? 2 : 4);
+  const int threads = std::max(32, ((a.hp + ppt - 1) / ppt + 31) / 32 * 32);
+  const int grid = static_cast<int>(std::min<int64_t>(rows, 148));
+  try {
+    switch (ppt) {
+      case 1: launch_ppt<1>(1, false, grid, threads, a, stream); break;
+      case 2: launch_ppt<2>(1, false, grid, threads, a, stream); break;
+      default: launch_ppt<4>(1, false, grid, threads, a, stream); break;
+    }
+  } catch (const std::exception& ex) {
+    return noalloc_fail(2, ex.what());
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return noalloc_fail(2, std::string("launch failed: ") + cudaGetErrorString(e));
+  return 0;
+}
+
+extern "C" const char* b200ar_noalloc_last_error(void) { return g_noalloc_err.c_str(); }
+
+extern "C" int64_t b200ar_noalloc_scratch_bytes(void) { return kNoallocScratch; }
