@@ -200,6 +200,26 @@ class CustomAllreduce:
         self._comm.ar_rmsnorm(x, residual, gamma, out, residual_out, float(eps), sel.variant_id(variant), int(ctas))
         return out, residual_out
 
+    def linear_all_reduce(self, x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+                          fused: bool = True) -> torch.Tensor:
+        """Row-parallel linear: ``sum over ranks of x_r @ w_r.T`` (bf16).
+
+        With ``fused`` (default) one persistent tcgen05 kernel computes the
+        partial tiles and pushes each one to its owner rank from the epilogue
+        (reduce-scatter), then the owners publish the reduced tiles
+        (all-gather). Shapes the fused kernel cannot serve fall back to the
+        tcgen05 GEMM followed by ``all_reduce``."""
+        from ..ops.gemm import error_word, linear
+
+        m, n = x.shape[0], w.shape[0]
+        if out is None:
+            out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+        if fused and self._comm is not None and self.world > 1 and self._comm.gemm_ar_supported(m, n):
+            self._comm.gemm_allreduce(x.contiguous(), w, out, error_word(x.device))
+            return out
+        partial = linear(x, w)
+        return self.all_reduce(partial, out=out)
+
     def _nccl(self, inp: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         if self.nccl_group is None:
             raise RuntimeError(

@@ -132,6 +132,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.attr("VARIANTS") = variants;
 
   m.def("ar_rmsnorm_slot_bytes", &ar_rmsnorm_slot_bytes);
+  m.def("gemm_ar_slot_bytes", &gemm_ar_slot_bytes);
   m.def("lamport_bytes", &lamport_bytes);
   m.def("workspace_bytes", &workspace_bytes, "bytes of one rank's workspace for a slot capacity");
   m.def("variant_slot_bytes", &variant_slot_bytes, "slot bytes a variant needs", py::arg("variant"),
@@ -237,6 +238,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       // The caller keeps `buf` alive and detaches it (set_nvls(None)) before dropping it.
       .def("set_nvls", [](Communicator& c, NvlsBuffer* b) { c.set_nvls(b); }, py::arg("buf").none(true))
       .def_property_readonly("has_nvls", &Communicator::has_nvls)
+      .def("gemm_ar_supported", [](Communicator& c, int64_t M, int64_t N) { return gemm_ar_supported(c, M, N); })
+      .def("gemm_allreduce",
+           [](Communicator& c, at::Tensor& a, at::Tensor& w, at::Tensor& out, at::Tensor& err) {
+             for (const at::Tensor* t : {&a, &w, &out})
+               TORCH_CHECK(t->is_cuda() && t->dim() == 2 && t->is_contiguous() && t->scalar_type() == at::kBFloat16,
+                           "fused GEMM + all-reduce takes contiguous 2-D bf16 CUDA tensors");
+             TORCH_CHECK(a.size(1) == w.size(1) && out.size(0) == a.size(0) && out.size(1) == w.size(0),
+                         "shape mismatch");
+             TORCH_CHECK(err.is_cuda() && err.scalar_type() == at::kInt, "err must be a CUDA int32 tensor");
+             const at::cuda::OptionalCUDAGuard guard(device_of(a));
+             gemm_allreduce(c, at::cuda::getCurrentCUDAStream().stream(), a.data_ptr(), w.data_ptr(), out.data_ptr(),
+                            a.size(0), w.size(0), a.size(1), err.data_ptr<int>());
+           })
       .def("check", &Communicator::check_status)
       .def("status",
            [](Communicator& c) {

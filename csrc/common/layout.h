@@ -32,6 +32,8 @@ constexpr int kMaxRanks = 8;
 constexpr int kMaxCTAs = 512;
 // Every collective call reserves this many barrier epochs.
 constexpr uint32_t kEpochsPerCall = 2;
+// Upper bound on output tiles of one fused GEMM + all-reduce call.
+constexpr int kMaxTiles = 4096;
 
 enum class DType : int { kFloat32 = 0, kFloat16 = 1, kBFloat16 = 2 };
 
@@ -69,6 +71,11 @@ struct alignas(256) Signal {
   // flags[cta][src]: highest epoch that rank `src` reached in CTA `cta`.
   // Written remotely by rank `src`, read locally.
   uint32_t flags[kMaxCTAs][kMaxRanks];
+  // Fused GEMM + all-reduce: tile_flags[t][src] = call epoch once rank `src`
+  // pushed its partial of tile t here; tile_ready[t] = call epoch once this
+  // rank (the tile's owner) published the reduced tile.
+  uint32_t tile_flags[kMaxTiles][kMaxRanks];
+  uint32_t tile_ready[kMaxTiles];
 };
 
 static_assert(sizeof(Signal) % 256 == 0, "Signal must keep 256-byte alignment of what follows");

@@ -18,4 +18,11 @@ int64_t ar_rmsnorm_slot_bytes(int variant, int64_t rows, int64_t hidden, int wor
 int ar_rmsnorm(Communicator& comm, cudaStream_t stream, const void* x, const void* residual, const void* gamma,
                void* y, void* residual_out, int64_t rows, int64_t hidden, float eps, int variant, int ctas);
 
+// Fused row-parallel linear + all-reduce: out = sum_ranks(A_r @ W_r^T)
+// (bf16 A [M, K], W [N, K], out [M, N]). `err` receives GEMM wait errors.
+int64_t gemm_ar_slot_bytes(int64_t M, int64_t N, int world);
+bool gemm_ar_supported(Communicator& comm, int64_t M, int64_t N);
+void gemm_allreduce(Communicator& comm, cudaStream_t stream, const void* A, const void* W, void* out, int64_t M,
+                    int64_t N, int64_t K, int* err);
+
 }  // namespace b200ar

@@ -42,7 +42,8 @@ struct StoreC {
   __nv_bfloat16* c;
   int64_t ldc;
   // Writes 32 consecutive columns [col, col + 32) of `row` (fp32 values v).
-  __device__ __forceinline__ void store(const Shape& s, int row, int col, const float* v) const {
+  __device__ __forceinline__ void store(const Shape& s, int row, int col, const float* v, int, int,
+                                        uint32_t) const {
     if (row >= s.M) return;
     uint32_t w[16];
 #pragma unroll
@@ -60,7 +61,13 @@ struct StoreC {
   // tile_done(s, tm, tn) is called by one epilogue thread once the whole tile
   // was stored, for epilogues that set kTileDone.
   static constexpr bool kTileDone = false;
-  __device__ __forceinline__ void tile_done(const Shape&, int, int) const {}
+  __device__ __forceinline__ void tile_done(const Shape&, int, int, uint32_t) const {}
+  // begin() runs on every thread before the roles split and returns a value
+  // handed to every other hook (fused epilogues read their call generation).
+  // post() runs on every thread after all tiles, TMEM already released.
+  static constexpr bool kPost = false;
+  __device__ __forceinline__ uint32_t begin() const { return 0; }
+  __device__ __forceinline__ void post(const Shape&, uint32_t, volatile int*) const {}
 };
 
 template <class Epi>
@@ -104,6 +111,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const uint32_t hook = epi.begin();
 
   if (warp == 0) {
     // ---------------- TMA producer
@@ -174,7 +182,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------- epilogue (warps 2..5)
     const int quarter = warp & 3;
     int local = 0;
-    for (int t = blockIdx.x; t < ntiles && !*s_err; t += gridDim.x, ++local) {
+    // No early exit on *s_err here: the four epilogue warps leave only through
+    // the same expired wait, so they stay in step at the named barrier.
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++local) {
       const int tm = t % s.tiles_m, tn = t / s.tiles_m;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1u;
@@ -191,7 +201,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         sm100::tmem_ld_32x32b_x32(taddr + c, r);
         sm100::tmem_ld_wait();
         const int col = tn * BN + c;
-        if (col < s.N) epi.store(s, row, col, reinterpret_cast<const float*>(r));
+        if (col < s.N) epi.store(s, row, col, reinterpret_cast<const float*>(r), tm, tn, hook);
       }
       sm100::tc_fence_before();
       __syncwarp();
@@ -199,7 +209,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if constexpr (Epi::kTileDone) {
         // All four epilogue warps finished this tile's stores.
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (warp == 2 && lane == 0) epi.tile_done(s, tm, tn);
+        if (warp == 2 && lane == 0) epi.tile_done(s, tm, tn, hook);
       }
     }
   }
@@ -210,6 +220,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem_base, TMEM_COLS);
   }
+  if constexpr (Epi::kPost) epi.post(s, hook, s_err);
   if (threadIdx.x == 0 && *s_err) atomicExch(err, kGemmTimeout);
 }
 

@@ -16,6 +16,9 @@ struct Shape;
 // with a box of box_rows x box_cols and 128-byte swizzle; no multicast.
 CUtensorMap make_tmap_bf16_2d(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows, int box_cols);
 
+// Tile counts for an M x N x K problem (validates the shape).
+gemm::Shape gemm_shape(int64_t M, int64_t N, int64_t K);
+
 // C[M, N] (bf16, row-major) = A[M, K] * B[N, K]^T. `err` is a device int that
 // receives a non-zero code if a bounded wait expired.
 void gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int* err,

@@ -271,3 +271,33 @@ def _nvls(rank, world):
 
 def test_nvls_multimem():
     run_ranks(_nvls, WORLD, backend="nccl")
+
+
+def _gemm_allreduce(rank, world):
+    # BASELINE config 4 (down projection): x [M, 3584] ~ N(0,1), W [8192, 3584] ~ N(0, 0.02).
+    from b200ar.ops.gemm import check_errors
+
+    comm = _comm(rank, max_size=160 << 20)
+    K, N = 3584, 8192
+    for M in (16, 128, 1024):
+        g = torch.Generator(device="cuda").manual_seed(1234 + rank + M)
+        x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+        w = (0.02 * torch.randn(N, K, generator=g, device="cuda")).to(torch.bfloat16)
+        part = (x.float() @ w.float().t())
+        ref = part.clone()
+        dist.all_reduce(ref)
+        for _ in range(3):
+            out = comm.linear_all_reduce(x, w)
+            torch.cuda.synchronize()
+            check_errors()
+            err = (out.float() - ref).abs().max().item()
+            assert err <= 2e-2 * ref.abs().max().item() + 2e-2, (M, err)
+        outs = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(outs, out)
+        assert all(torch.equal(o, outs[0]) for o in outs), "ranks disagree"
+    comm.check()
+    comm.close()
+
+
+def test_gemm_allreduce_fused():
+    run_ranks(_gemm_allreduce, WORLD, backend="nccl")
