@@ -220,6 +220,27 @@ class CustomAllreduce:
         partial = linear(x, w)
         return self.all_reduce(partial, out=out)
 
+    def all_gather_linear(self, x_shard: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+                          fused: bool = True) -> torch.Tensor:
+        """Column-parallel linear on sequence-sharded input:
+        ``concat over ranks of x_shard (rows) @ w.T``. Fused, the GEMM's TMA
+        producer reads every shard straight from its owner over NVLink; other
+        shapes fall back to an all-gather followed by the tcgen05 GEMM."""
+        from ..ops.gemm import error_word, linear
+
+        rows, k = x_shard.shape
+        if out is None:
+            out = torch.empty(rows * self.world, w.shape[0], dtype=torch.bfloat16, device=x_shard.device)
+        if fused and self._comm is not None and self._comm.ag_gemm_supported(rows, k):
+            self._comm.ag_gemm(x_shard.contiguous(), w, out, error_word(x_shard.device))
+            return out
+        full = torch.empty(rows * self.world, k, dtype=x_shard.dtype, device=x_shard.device)
+        if self.world > 1:
+            dist.all_gather_into_tensor(full, x_shard.contiguous(), group=self.nccl_group)
+        else:
+            full.copy_(x_shard)
+        return linear(full, w, out=out)
+
     def _nccl(self, inp: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         if self.nccl_group is None:
             raise RuntimeError(

@@ -251,6 +251,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
              gemm_allreduce(c, at::cuda::getCurrentCUDAStream().stream(), a.data_ptr(), w.data_ptr(), out.data_ptr(),
                             a.size(0), w.size(0), a.size(1), err.data_ptr<int>());
            })
+      .def("ag_gemm_supported",
+           [](Communicator& c, int64_t rows, int64_t K) { return ag_gemm_supported(c, rows, K); })
+      .def("ag_gemm",
+           [](Communicator& c, at::Tensor& x, at::Tensor& w, at::Tensor& y, at::Tensor& err) {
+             for (const at::Tensor* t : {&x, &w, &y})
+               TORCH_CHECK(t->is_cuda() && t->dim() == 2 && t->is_contiguous() && t->scalar_type() == at::kBFloat16,
+                           "all-gather GEMM takes contiguous 2-D bf16 CUDA tensors");
+             TORCH_CHECK(x.size(1) == w.size(1) && y.size(0) == x.size(0) * c.world() && y.size(1) == w.size(0),
+                         "shape mismatch");
+             const at::cuda::OptionalCUDAGuard guard(device_of(x));
+             ag_gemm(c, at::cuda::getCurrentCUDAStream().stream(), x.data_ptr(), w.data_ptr(), y.data_ptr(),
+                     x.size(0), w.size(0), x.size(1), err.data_ptr<int>());
+           })
       .def("check", &Communicator::check_status)
       .def("status",
            [](Communicator& c) {

@@ -25,4 +25,10 @@ bool gemm_ar_supported(Communicator& comm, int64_t M, int64_t N);
 void gemm_allreduce(Communicator& comm, cudaStream_t stream, const void* A, const void* W, void* out, int64_t M,
                     int64_t N, int64_t K, int* err);
 
+// Column-parallel linear with the all-gather fused into the GEMM prologue:
+// Y[rows_per_rank * world, N] = concat_ranks(x_shard) @ W^T.
+bool ag_gemm_supported(Communicator& comm, int64_t rows_per_rank, int64_t K);
+void ag_gemm(Communicator& comm, cudaStream_t stream, const void* x_shard, const void* W, void* Y,
+             int64_t rows_per_rank, int64_t N, int64_t K, int* err);
+
 }  // namespace b200ar

@@ -169,7 +169,7 @@ void gemm_allreduce(Communicator& comm, cudaStream_t stream, const void* A, cons
                                              << " tiles and " << gemm_ar_slot_bytes(M, N, comm.world())
                                              << " slot bytes (capacity " << comm.slot_capacity() << ")");
   const gemm::Shape s = gemm_shape(M, N, K);
-  const CUtensorMap ta = make_tmap_bf16_2d(A, M, K, K, gemm::BM, gemm::BK);
+  const gemm::TmapA ta{make_tmap_bf16_2d(A, M, K, K, gemm::BM, gemm::BK)};
   const CUtensorMap tb = make_tmap_bf16_2d(W, N, K, K, gemm::BN, gemm::BK);
   ArEpi epi{};
   comm.fill_ctx(&epi.ctx);

@@ -84,7 +84,7 @@ void gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int6
                int max_ctas) {
   const gemm::Shape s = gemm_shape(M, N, K);
   B200AR_CHECK(N % 8 == 0 && reinterpret_cast<uintptr_t>(C) % 16 == 0, "C must have 16-byte aligned rows");
-  const CUtensorMap ta = make_tmap_bf16_2d(A, M, K, K, gemm::BM, gemm::BK);
+  const gemm::TmapA ta{make_tmap_bf16_2d(A, M, K, K, gemm::BM, gemm::BK)};
   const CUtensorMap tb = make_tmap_bf16_2d(B, N, K, K, gemm::BN, gemm::BK);
   gemm::StoreC epi{static_cast<__nv_bfloat16*>(C), N};
   auto kern = gemm::gemm_kernel<gemm::StoreC>;

@@ -70,10 +70,19 @@ struct StoreC {
   __device__ __forceinline__ void post(const Shape&, uint32_t, volatile int*) const {}
 };
 
-template <class Epi>
+// A-operand source: one tensor map, 128-row boxes.
+struct TmapA {
+  CUtensorMap map;
+  __device__ __forceinline__ void prefetch() const { sm100::prefetch_tmap(&map); }
+  __device__ __forceinline__ void load(void* dst, uint64_t* bar, int kx, int tm) const {
+    sm100::tma_load_2d(dst, &map, bar, kx, tm * BM);
+  }
+};
+
+template <class Epi, class ASrc = TmapA>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, Shape s,
-                Epi epi, int* err) {
+    gemm_kernel(const __grid_constant__ ASrc asrc, const __grid_constant__ CUtensorMap tmap_b, Shape s, Epi epi,
+                int* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -100,7 +109,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     *s_err = 0;
     sm100::fence_barrier_init();
-    sm100::prefetch_tmap(&tmap_a);
+    asrc.prefetch();
     sm100::prefetch_tmap(&tmap_b);
   }
   if (warp == 1) {
@@ -129,7 +138,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           sm100::mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          sm100::tma_load_2d(sA + stage * A_BYTES, &tmap_a, &full[stage], kb * BK, tm * BM);
+          asrc.load(sA + stage * A_BYTES, &full[stage], kb * BK, tm);
           sm100::tma_load_2d(sB + stage * B_BYTES, &tmap_b, &full[stage], kb * BK, tn * BN);
           issued[stage] = true;
           issued_phase[stage] = phase;

@@ -19,6 +19,9 @@ CUtensorMap make_tmap_bf16_2d(const void* base, int64_t rows, int64_t cols, int6
 // Tile counts for an M x N x K problem (validates the shape).
 gemm::Shape gemm_shape(int64_t M, int64_t N, int64_t K);
 
+// Persistent grid size for a shape (at most one CTA per SM, `max_ctas` if > 0).
+int gemm_grid(const gemm::Shape& s, int max_ctas);
+
 // C[M, N] (bf16, row-major) = A[M, K] * B[N, K]^T. `err` is a device int that
 // receives a non-zero code if a bounded wait expired.
 void gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int* err,

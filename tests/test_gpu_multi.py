@@ -301,3 +301,32 @@ def _gemm_allreduce(rank, world):
 
 def test_gemm_allreduce_fused():
     run_ranks(_gemm_allreduce, WORLD, backend="nccl")
+
+
+def _ag_gemm(rank, world):
+    from b200ar.ops.gemm import check_errors
+
+    comm = _comm(rank, max_size=64 << 20)
+    K, N = 8192, 3584
+    for rows in (16, 128, 512):
+        g = torch.Generator(device="cuda").manual_seed(99 + rank + rows)
+        x = torch.randn(rows, K, generator=g, device="cuda").to(torch.bfloat16)
+        w = (0.02 * torch.randn(N, K, generator=torch.Generator(device="cuda").manual_seed(5 + rank),
+                                device="cuda")).to(torch.bfloat16)
+        full = torch.empty(rows * world, K, dtype=torch.bfloat16, device="cuda")
+        dist.all_gather_into_tensor(full, x)
+        ref = full.float() @ w.float().t()
+        for _ in range(3):
+            y = comm.all_gather_linear(x, w)
+            torch.cuda.synchronize()
+            check_errors()
+            err = (y.float() - ref).abs().max().item()
+            assert err <= 1e-2 * ref.abs().max().item() + 1e-2, (rows, err)
+        # Interleave with all-reduces (shared generation / slots).
+        comm.all_reduce(x)
+    comm.check()
+    comm.close()
+
+
+def test_allgather_gemm_fused():
+    run_ranks(_ag_gemm, WORLD, backend="nccl")
