@@ -35,13 +35,44 @@ def check_errors(device=None) -> None:
             raise RuntimeError(f"tcgen05 GEMM on cuda:{idx} reported error {v} (a bounded wait expired)")
 
 
-def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None, max_ctas: int = 0) -> torch.Tensor:
-    """``x @ w.T`` (bf16). ``x``: [..., K]; ``w``: [N, K]."""
+_SKINNY: Dict[int, dict] = {}
+
+
+def _skinny_workspace(device, splits: int, m: int, n: int):
+    """Per-device split-K scratch: fp32 partials and zeroed arrival counters
+    (reused by every decode GEMM on that device; calls are stream-ordered)."""
+    idx = torch.device(device).index or 0
+    ws = _SKINNY.setdefault(idx, {})
+    need = splits * m * n
+    if ws.get("partials") is None or ws["partials"].numel() < need:
+        ws["partials"] = torch.empty(max(need, 1 << 20), dtype=torch.float32, device=device)
+    blocks = (n + 127) // 128
+    if ws.get("counters") is None or ws["counters"].numel() < blocks:
+        ws["counters"] = torch.zeros(max(blocks, 1024), dtype=torch.int32, device=device)
+    if "sms" not in ws:
+        ws["sms"] = torch.cuda.get_device_properties(device).multi_processor_count
+    return ws
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None, max_ctas: int = 0,
+           skinny: Optional[bool] = None) -> torch.Tensor:
+    """``x @ w.T`` (bf16). ``x``: [..., K]; ``w``: [N, K]. Rows <= 128 use the
+    split-K decode kernel unless ``skinny=False``."""
     shp = x.shape
     x2 = x.reshape(-1, shp[-1])
     if not x2.is_contiguous():
         x2 = x2.contiguous()
+    m, n = x2.shape[0], w.shape[0]
     if out is None:
-        out = torch.empty(x2.shape[0], w.shape[0], dtype=torch.bfloat16, device=x.device)
-    _C.gemm_bf16(x2, w, out.view(x2.shape[0], w.shape[0]), error_word(x.device), max_ctas)
-    return out.view(*shp[:-1], w.shape[0])
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+    out2 = out.view(m, n)
+    if skinny is None:
+        skinny = m <= 128
+    if skinny:
+        ws = _skinny_workspace(x.device, 1, m, n)
+        splits = _C.skinny_splits(n, x2.shape[1], ws["sms"])
+        ws = _skinny_workspace(x.device, splits, m, n)
+        _C.gemm_skinny(x2, w, out2, ws["partials"], ws["counters"], error_word(x.device), splits)
+    else:
+        _C.gemm_bf16(x2, w, out2, error_word(x.device), max_ctas)
+    return out.view(*shp[:-1], n)

@@ -25,7 +25,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--shapes", default="16x8192x3584,128x8192x3584,1024x8192x3584,8192x8192x3584,8192x8192x8192")
+    ap.add_argument("--shapes", default="1x1280x8192,8x1280x8192,64x1280x8192,1x8192x1024,8x7168x8192,64x7168x8192,8x8192x3584,64x8192x3584,16x8192x3584,128x8192x3584,1024x8192x3584,8192x8192x3584,8192x8192x8192")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     flush = L2Flusher(dev, lead_us=20)

@@ -1,0 +1,257 @@
+"""Stress suite for b200ar (multi-GPU), a port of the reference's eleven
+scenarios (stress_test.py:100-377) plus a long random-size run.
+
+Every scenario checks results against closed-form or fp32 oracles and reports
+PASS/FAIL per rank 0; the process exits non-zero on any failure.
+
+  t1 rapid_fire          10K eager all-reduces of bf16 [1, 7168]
+  t2 varying_sizes       numel 16 .. 14336 bf16
+  t3 unique_values       200x fp32 7168 with per-element distinct values
+  t4 back_to_back        5K calls with values changing every call
+  t5 alternating         1K calls alternating 16 and 7168 elements
+  t6 dtypes              bf16 / fp16 / fp32 x 100
+  t7 decode_step         50 steps x 61 layers x 2 all-reduces with torch ops between
+  t8 continuous_batching batch 1..32 x 7168, interleaved
+  t9 sustained_decode    200 tokens x 122 all-reduces
+  t10 cuda_graph         capture 10 all-reduces, replay 500
+  t11 cuda_graph_decode  capture 61 x (AR, copy, mul, mul, AR), replay 200
+  t12 random_sizes       --random-iters calls, sizes uniform in 1 KB .. 64 MB,
+                         random variants, oracle check every 1000 calls
+
+    python -m torch.distributed.run --nproc-per-node N bench/stress.py [--random-iters 100000]
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+from b200ar import CustomAllreduce  # noqa: E402
+
+HIDDEN = 7168
+LAYERS = 61
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--random-iters", type=int, default=100000)
+    ap.add_argument("--only", default="")
+    args = ap.parse_args()
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    gloo = dist.new_group(backend="gloo")
+    dev = torch.device("cuda", local)
+    comm = CustomAllreduce(group=gloo, device=dev, nccl_group=dist.group.WORLD, max_size=64 << 20)
+    ws = world
+    tri = ws * (ws + 1) / 2.0
+    results = {}
+
+    def ar(x, out=None, variant="auto"):
+        return comm.all_reduce(x, out=out, variant=variant)
+
+    def check(name, ok, extra=""):
+        flag = torch.tensor([1 if ok else 0], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        ok = bool(flag.item())
+        results[name] = ok
+        if rank == 0:
+            print(f"  {name:<22s} {'PASS' if ok else 'FAIL'} {extra}", flush=True)
+
+    def t1():
+        x = torch.full((1, HIDDEN), float(rank + 1), dtype=torch.bfloat16, device=dev)
+        out = torch.empty_like(x)
+        t0 = time.perf_counter()
+        for _ in range(10000):
+            ar(x, out)
+        torch.cuda.synchronize()
+        el = time.perf_counter() - t0
+        check("rapid_fire", bool((out.float() - tri).abs().max() < 0.5), f"{el / 10000 * 1e6:.1f} us/call host")
+
+    def t2():
+        ok = True
+        for n in [16, 32, 64, 128, 256, 512, 1024, 2048, 4096, 7168, 8192, 14336]:
+            x = torch.full((n,), float(rank + 1), dtype=torch.bfloat16, device=dev)
+            ok &= bool((ar(x).float() - tri).abs().max() < 0.5)
+        check("varying_sizes", ok)
+
+    def t3():
+        ok = True
+        base = torch.arange(HIDDEN, dtype=torch.float32, device=dev) * 0.001
+        for i in range(200):
+            x = base + (i * ws + rank + 1) * 0.01
+            exp = sum(base + (i * ws + r + 1) * 0.01 for r in range(ws))
+            ok &= bool((ar(x) - exp).abs().max() < 0.1)
+        check("unique_values", ok)
+
+    def t4():
+        out = None
+        for i in range(5000):
+            x = torch.full((1, HIDDEN), float(rank + 1) + i * 0.001, dtype=torch.bfloat16, device=dev)
+            out = ar(x)
+        torch.cuda.synchronize()
+        last = sum(float(r + 1) + 4999 * 0.001 for r in range(ws))
+        check("back_to_back", bool((out.float() - last).abs().max() < 1.0))
+
+    def t5():
+        out = None
+        for i in range(1000):
+            n = 16 if i % 2 == 0 else HIDDEN
+            out = ar(torch.full((n,), float(rank + 1), dtype=torch.bfloat16, device=dev))
+        check("alternating", bool((out.float() - tri).abs().max() < 0.5))
+
+    def t6():
+        ok = True
+        for dt in (torch.bfloat16, torch.float16, torch.float32):
+            x = torch.full((1, 1024), float(rank + 1), dtype=dt, device=dev)
+            out = torch.empty_like(x)
+            for _ in range(100):
+                ar(x, out)
+            ok &= bool((out.float() - tri).abs().max() < 0.5)
+        check("dtypes", ok)
+
+    def t7():
+        x = torch.full((1, HIDDEN), float(rank + 1), dtype=torch.bfloat16, device=dev)
+        out = torch.empty_like(x)
+        scratch = torch.empty_like(x)
+        t0 = time.perf_counter()
+        for _ in range(50):
+            for _ in range(LAYERS):
+                x.fill_(float(rank + 1))
+                ar(x, out)
+                scratch.copy_(out)
+                scratch.mul_(1.0 / tri)
+                scratch.mul_(float(rank + 1))
+                ar(scratch, out)
+        torch.cuda.synchronize()
+        el = time.perf_counter() - t0
+        check("decode_step", bool((out.float() - tri).abs().max() < 1.0), f"{el / 50 * 1e3:.2f} ms/step host")
+
+    def t8():
+        ok = True
+        for step in range(40):
+            bs = [1, 2, 3, 4, 8, 16, 32][step % 7]
+            x = torch.full((bs, HIDDEN), float(rank + 1), dtype=torch.bfloat16, device=dev)
+            out = torch.empty_like(x)
+            for _ in range(2 * LAYERS):
+                ar(x, out)
+            ok &= bool((out.float() - tri).abs().max() < 0.5)
+        check("continuous_batching", ok)
+
+    def t9():
+        x = torch.empty(1, HIDDEN, dtype=torch.bfloat16, device=dev)
+        out = torch.empty_like(x)
+        for _ in range(200):
+            for _ in range(2 * LAYERS):
+                x.fill_(float(rank + 1))
+                ar(x, out)
+        check("sustained_decode", bool((out.float() - tri).abs().max() < 1.0))
+
+    def graph_of(fn):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        return g
+
+    def t10():
+        gi = torch.full((1, HIDDEN), float(rank + 1), dtype=torch.bfloat16, device=dev)
+        go = torch.empty_like(gi)
+
+        def body():
+            for _ in range(10):
+                ar(gi, go)
+
+        g = graph_of(body)
+        for _ in range(500):
+            gi.fill_(float(rank + 1))
+            g.replay()
+        torch.cuda.synchronize()
+        check("cuda_graph", bool((go.float() - tri).abs().max() < 0.5))
+
+    def t11():
+        gi = torch.full((1, HIDDEN), float(rank + 1), dtype=torch.bfloat16, device=dev)
+        go = torch.empty_like(gi)
+        sc = torch.empty_like(gi)
+
+        def body():
+            for _ in range(LAYERS):
+                ar(gi, go)
+                sc.copy_(go)
+                sc.mul_(1.0 / tri)
+                sc.mul_(float(rank + 1))
+                ar(sc, go)
+
+        g = graph_of(body)
+        for _ in range(200):
+            gi.fill_(float(rank + 1))
+            g.replay()
+        torch.cuda.synchronize()
+        check("cuda_graph_decode", bool((go.float() - tri).abs().max() < 1.0))
+
+    def t12():
+        gen = torch.Generator().manual_seed(2024)
+        variants = ["auto", "auto", "lamport", "oneshot_push", "oneshot_pull", "twoshot"]
+        big = torch.empty(32 << 20, dtype=torch.bfloat16, device=dev)  # 64 MB
+        big.uniform_(-1, 1, generator=torch.Generator(device=dev).manual_seed(rank))
+        out = torch.empty_like(big)
+        ok = True
+        checked = 0
+        t0 = time.perf_counter()
+        for i in range(args.random_iters):
+            nbytes = int(torch.randint(1 << 10, (64 << 20) + 1, (1,), generator=gen)) // 16 * 16
+            v = variants[int(torch.randint(len(variants), (1,), generator=gen))]
+            if v == "lamport" and nbytes > comm.lamport_capacity:
+                v = "auto"
+            if v == "oneshot_push" and nbytes * ws > comm.slot_capacity:
+                v = "auto"
+            n = nbytes // 2
+            ar(big[:n], out[:n], variant=v)
+            if i % 1000 == 999:
+                torch.cuda.synchronize()
+                ref = big[:n].float()
+                dist.all_reduce(ref)
+                ok &= bool((out[:n].float() - ref).abs().max() <= 2e-2 * ws)
+                checked += 1
+        torch.cuda.synchronize()
+        comm.check()
+        el = time.perf_counter() - t0
+        check("random_sizes", ok, f"{args.random_iters} calls, {checked} oracle checks, {el:.1f} s")
+
+    tests = [t1, t2, t3, t4, t5, t6, t7, t8, t9, t10, t11, t12]
+    for t in tests:
+        if args.only and t.__name__ not in args.only.split(","):
+            continue
+        dist.barrier()
+        try:
+            t()
+        except Exception as e:  # noqa: BLE001 - reported as a failure
+            results[t.__name__] = False
+            print(f"rank {rank}: {t.__name__} raised {e!r}", flush=True)
+    comm.close()
+    ok = all(results.values())
+    if rank == 0:
+        print(f"\n{'ALL STRESS TESTS PASSED' if ok else 'SOME STRESS TESTS FAILED'}", flush=True)
+    torch.cuda.synchronize()
+    dist.barrier(group=gloo)
+    sys.stdout.flush()
+    os._exit(0 if ok else 1)
+
+
+if __name__ == "__main__":
+    main()

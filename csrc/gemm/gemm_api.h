@@ -27,4 +27,12 @@ int gemm_grid(const gemm::Shape& s, int max_ctas);
 void gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int* err,
                cudaStream_t stream, int max_ctas = 0);
 
+// Decode GEMM for M <= 128 (swap-AB, split-K over `splits` CTAs per 128-row
+// weight block). `partials` (fp32 [splits, M, N]) and `counters` (zeroed
+// uint32 [ceil(N / 128)]) are needed when splits > 1; calls that share them
+// must be ordered on one stream.
+int skinny_splits(int64_t N, int64_t K, int sms);
+void gemm_skinny(const void* x, const void* w, void* out, float* partials, unsigned* counters, int64_t M, int64_t N,
+                 int64_t K, int splits, int* err, cudaStream_t stream);
+
 }  // namespace b200ar

@@ -1,0 +1,247 @@
+// Skinny (decode) GEMM for sm_100a: out[M, N] = x[M, K] * W[N, K]^T with M <= 128.
+//
+// Decode GEMMs stream the weights once and do little math per byte, so the
+// work must be spread over every SM. The kernel swaps the operands (the
+// weight rows become the 128-wide UMMA M dimension, the padded batch the UMMA
+// N dimension, 16..128) and splits K over `splits` CTAs:
+//   CTA (b, s): weight rows [128 b, 128 b + 128), K blocks of split s.
+//   warp 0: TMA producer (W tile 128 x 64, x tile MP x 64, 6-stage ring)
+//   warp 1: tcgen05.mma issuer, accumulator 128 lanes x MP columns in TMEM
+//   warps 0-3: epilogue, thread = one weight row n, MP batch columns.
+// With one split the bf16 result is written directly. Otherwise each CTA
+// writes its fp32 partial to `partials[s][m][n]`, and the last CTA of a row
+// block (per-block arrival counter) sums the partials in split order and
+// writes bf16, so results do not depend on arrival order. The counter is
+// reset by that last CTA for the next call.
+#include <cuda.h>
+
+#include <algorithm>
+#include <stdexcept>
+
+#include "../common/check.h"
+#include "gemm_api.h"
+#include "tcgen05.cuh"
+
+namespace b200ar {
+
+namespace {
+
+constexpr int SBM = 128;
+constexpr int SBK = 64;
+constexpr int SSTAGES = 6;
+constexpr int STHREADS = 128;
+
+template <int MP>
+struct SkinnyCfg {
+  static constexpr uint32_t W_BYTES = SBM * SBK * 2;
+  static constexpr uint32_t X_BYTES = MP * SBK * 2;
+  static constexpr uint32_t STAGE = W_BYTES + X_BYTES;
+  static constexpr size_t SMEM = SSTAGES * STAGE + 1024 + 256;
+  static constexpr uint32_t TMEM_COLS = MP < 32 ? 32 : MP;
+};
+
+struct SkinnyArgs {
+  __nv_bfloat16* out;
+  float* partials;      // [splits, M, N] when splits > 1
+  unsigned* counters;   // [N / 128] arrival counters, zero between calls
+  int M, N, K;
+  int nblocks, splits, kblocks;
+};
+
+template <int MP>
+__global__ void __launch_bounds__(STHREADS, 1)
+    skinny_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                  SkinnyArgs a, int* err) {
+  using C = SkinnyCfg<MP>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sW = smem;
+  uint8_t* sX = smem + SSTAGES * C::W_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SSTAGES * C::STAGE);
+  uint64_t* empty = full + SSTAGES;
+  uint64_t* done = empty + SSTAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* s_err = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* s_last = const_cast<int*>(s_err) + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x % a.nblocks;
+  const int sp = blockIdx.x / a.nblocks;
+  const int kb0 = static_cast<int>((static_cast<int64_t>(a.kblocks) * sp) / a.splits);
+  const int kb1 = static_cast<int>((static_cast<int64_t>(a.kblocks) * (sp + 1)) / a.splits);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < SSTAGES; ++i) {
+      sm100::mbar_init(&full[i], 1);
+      sm100::mbar_init(&empty[i], 1);
+    }
+    sm100::mbar_init(done, 1);
+    *s_err = 0;
+    sm100::fence_barrier_init();
+    sm100::prefetch_tmap(&tmap_w);
+    sm100::prefetch_tmap(&tmap_x);
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(tmem_slot, C::TMEM_COLS);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (sm100::elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool issued[SSTAGES] = {};
+      uint32_t iphase[SSTAGES] = {};
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!sm100::mbar_wait(&empty[stage], phase ^ 1u)) {
+          *s_err = 1;
+          break;
+        }
+        sm100::mbar_arrive_expect_tx(&full[stage], C::STAGE);
+        sm100::tma_load_2d(sW + stage * C::W_BYTES, &tmap_w, &full[stage], kb * SBK, b * SBM);
+        sm100::tma_load_2d(sX + stage * C::X_BYTES, &tmap_x, &full[stage], kb * SBK, 0);
+        issued[stage] = true;
+        iphase[stage] = phase;
+        if (++stage == SSTAGES) stage = 0, phase ^= 1u;
+      }
+      for (int i = 0; i < SSTAGES; ++i)
+        if (issued[i]) sm100::mbar_wait(&full[i], iphase[i]);
+    }
+  } else if (warp == 1) {
+    if (sm100::elect_one()) {
+      constexpr uint32_t idesc = sm100::idesc_bf16_f32(SBM, MP);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!sm100::mbar_wait(&full[stage], phase)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        const uint64_t dw = sm100::smem_desc_sw128(sW + stage * C::W_BYTES);
+        const uint64_t dx = sm100::smem_desc_sw128(sX + stage * C::X_BYTES);
+#pragma unroll
+        for (int k = 0; k < SBK / 16; ++k) sm100::mma_bf16(tmem, dw + 2 * k, dx + 2 * k, idesc, (kb > kb0 || k > 0));
+        sm100::mma_commit(&empty[stage]);
+        if (++stage == SSTAGES) stage = 0, phase ^= 1u;
+      }
+      if (!ok) *s_err = 1;
+      sm100::mma_commit(done);  // also fires when no MMA was issued
+    }
+  }
+  __syncwarp();
+
+  // ---------------- epilogue: all 4 warps; thread = weight row n
+  const bool have = kb1 > kb0;
+  const bool ok = sm100::mbar_wait(done, 0);
+  if (!ok) *s_err = 1;
+  sm100::tc_fence_after();
+  const int n = b * SBM + warp * 32 + lane;
+  // Partial (or final) values leave TMEM 32 batch columns at a time.
+  constexpr int CH = MP < 32 ? MP : 32;
+  if (ok) {
+#pragma unroll 1
+    for (int c = 0; c < MP; c += CH) {
+      uint32_t r[32];
+      sm100::tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c, r);
+      sm100::tmem_ld_wait();
+      if (n < a.N) {
+#pragma unroll
+        for (int i = 0; i < CH; ++i) {
+          const int m = c + i;
+          if (m < a.M) {
+            const float v = have ? __uint_as_float(r[i]) : 0.f;
+            if (a.splits == 1)
+              a.out[static_cast<int64_t>(m) * a.N + n] = __float2bfloat16_rn(v);
+            else
+              a.partials[(static_cast<int64_t>(sp) * a.M + m) * a.N + n] = v;
+          }
+        }
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+  if (!ok) {
+    if (threadIdx.x == 0) atomicExch(err, 1);
+    return;
+  }
+  if (a.splits == 1) return;
+  // Split-K: the last CTA of this row block sums the partials in split order.
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) *s_last = atomicAdd(&a.counters[b], 1u) == static_cast<unsigned>(a.splits - 1);
+  __syncthreads();
+  if (!*s_last) return;
+  __threadfence();
+  if (n < a.N) {
+    for (int m = 0; m < a.M; ++m) {
+      float s = 0.f;
+      for (int q = 0; q < a.splits; ++q) s += __ldcg(&a.partials[(static_cast<int64_t>(q) * a.M + m) * a.N + n]);
+      a.out[static_cast<int64_t>(m) * a.N + n] = __float2bfloat16_rn(s);
+    }
+  }
+  if (threadIdx.x == 0) a.counters[b] = 0;
+}
+
+template <int MP>
+void launch_skinny(const void* x, const void* w, void* out, float* partials, unsigned* counters, int64_t M, int64_t N,
+                   int64_t K, int splits, int* err, cudaStream_t stream) {
+  using C = SkinnyCfg<MP>;
+  const CUtensorMap tw = make_tmap_bf16_2d(w, N, K, K, SBM, SBK);
+  const CUtensorMap tx = make_tmap_bf16_2d(x, M, K, K, MP, SBK);
+  SkinnyArgs a{};
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.partials = partials;
+  a.counters = counters;
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.nblocks = static_cast<int>((N + SBM - 1) / SBM);
+  a.kblocks = static_cast<int>((K + SBK - 1) / SBK);
+  a.splits = splits;
+  auto kern = skinny_kernel<MP>;
+  static bool attr = false;
+  if (!attr) {
+    B200AR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM)));
+    attr = true;
+  }
+  kern<<<a.nblocks * splits, STHREADS, C::SMEM, stream>>>(tw, tx, a, err);
+  B200AR_CUDA(cudaGetLastError());
+}
+
+}  // namespace
+
+int skinny_splits(int64_t N, int64_t K, int sms) {
+  const int64_t nblocks = (N + SBM - 1) / SBM;
+  const int64_t kblocks = (K + SBK - 1) / SBK;
+  int64_t s = std::max<int64_t>(1, sms / nblocks);
+  s = std::min<int64_t>(s, std::max<int64_t>(1, kblocks / 2));  // at least two K blocks per split
+  return static_cast<int>(std::min<int64_t>(s, 32));
+}
+
+void gemm_skinny(const void* x, const void* w, void* out, float* partials, unsigned* counters, int64_t M, int64_t N,
+                 int64_t K, int splits, int* err, cudaStream_t stream) {
+  B200AR_CHECK(M >= 1 && M <= SBM, "skinny GEMM serves 1 <= M <= 128, got " << M);
+  B200AR_CHECK(K % 8 == 0 && N % 8 == 0, "K and N must be multiples of 8");
+  B200AR_CHECK(splits >= 1 && (splits == 1 || (partials && counters)), "split-K needs partials and counters");
+  if (M <= 16)
+    launch_skinny<16>(x, w, out, partials, counters, M, N, K, splits, err, stream);
+  else if (M <= 32)
+    launch_skinny<32>(x, w, out, partials, counters, M, N, K, splits, err, stream);
+  else if (M <= 64)
+    launch_skinny<64>(x, w, out, partials, counters, M, N, K, splits, err, stream);
+  else
+    launch_skinny<128>(x, w, out, partials, counters, M, N, K, splits, err, stream);
+}
+
+}  // namespace b200ar

@@ -33,4 +33,26 @@ void register_ops(py::module& m) {
       },
       "C = A @ B^T with the tcgen05 GEMM (bf16 in/out, fp32 accumulate)", py::arg("a"), py::arg("b"), py::arg("c"),
       py::arg("err"), py::arg("max_ctas") = 0);
+  m.def("skinny_splits", &b200ar::skinny_splits, py::arg("n"), py::arg("k"), py::arg("sms"));
+  m.def(
+      "gemm_skinny",
+      [](const at::Tensor& x, const at::Tensor& w, at::Tensor& out, at::Tensor& partials, at::Tensor& counters,
+         at::Tensor& err, int splits) {
+        check_bf16_2d(x, "x");
+        check_bf16_2d(w, "W");
+        check_bf16_2d(out, "out");
+        TORCH_CHECK(x.size(1) == w.size(1) && out.size(0) == x.size(0) && out.size(1) == w.size(0), "shape mismatch");
+        TORCH_CHECK(partials.is_cuda() && partials.scalar_type() == at::kFloat &&
+                        partials.numel() >= (splits > 1 ? splits * x.size(0) * w.size(0) : 0),
+                    "partials must be a CUDA float32 tensor of splits * M * N elements");
+        TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt &&
+                        counters.numel() >= (w.size(0) + 127) / 128,
+                    "counters must be a zeroed CUDA int32 tensor of ceil(N / 128) elements");
+        const at::cuda::OptionalCUDAGuard guard(device_of(x));
+        b200ar::gemm_skinny(x.data_ptr(), w.data_ptr(), out.data_ptr(), partials.data_ptr<float>(),
+                            reinterpret_cast<unsigned*>(counters.data_ptr<int>()), x.size(0), w.size(0), x.size(1),
+                            splits, err.data_ptr<int>(), at::cuda::getCurrentCUDAStream().stream());
+      },
+      "decode GEMM (M <= 128): out = x @ W^T, swap-AB tcgen05 with split-K", py::arg("x"), py::arg("w"),
+      py::arg("out"), py::arg("partials"), py::arg("counters"), py::arg("err"), py::arg("splits"));
 }

@@ -40,3 +40,20 @@ def test_gemm_repeated_and_capped_grid():
         torch.cuda.synchronize()
         check_errors()
         torch.testing.assert_close(out.float(), ref.float(), atol=0.5, rtol=2e-2)
+
+
+@pytest.mark.parametrize("m", [1, 8, 16, 17, 32, 64, 100, 128])
+@pytest.mark.parametrize("n,k", [(1280, 8192), (8192, 1024), (7168, 8192), (8192, 3584), (264, 136)])
+def test_skinny_gemm_matches_fp32(m, n, k):
+    from b200ar.ops.gemm import check_errors, linear
+
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    a = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+    w = (0.02 * torch.randn(n, k, generator=g, device="cuda")).to(torch.bfloat16)
+    for _ in range(2):  # the split-K counters must be reset by the first call
+        out = linear(a, w, skinny=True)
+        torch.cuda.synchronize()
+        check_errors()
+        ref = a.float() @ w.float().t()
+        err = (out.float() - ref).abs().max().item()
+        assert err <= 1e-2 * ref.abs().max().item() + 1e-2, (m, n, k, err)
