@@ -183,11 +183,51 @@ __global__ void __launch_bounds__(STHREADS, 1)
   __syncthreads();
   if (!*s_last) return;
   __threadfence();
-  if (n < a.N) {
-    for (int m = 0; m < a.M; ++m) {
-      float s = 0.f;
-      for (int q = 0; q < a.splits; ++q) s += __ldcg(&a.partials[(static_cast<int64_t>(q) * a.M + m) * a.N + n]);
-      a.out[static_cast<int64_t>(m) * a.N + n] = __float2bfloat16_rn(s);
+  {
+    // 16-byte loads: thread item = (row m, 4 consecutive columns of this
+    // block); four items and four splits of loads in flight, sums in split order.
+    const int64_t sstride = static_cast<int64_t>(a.M) * a.N;
+    const int items = a.M * (SBM / 4);
+    for (int i0 = threadIdx.x; i0 < items; i0 += 4 * STHREADS) {
+      float4 acc[4];
+      int64_t off[4];
+      bool on[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int it = i0 + j * STHREADS;
+        const int m = it / (SBM / 4), c = (it % (SBM / 4)) * 4;
+        const int col = b * SBM + c;
+        on[j] = it < items && col < a.N;
+        off[j] = static_cast<int64_t>(m) * a.N + col;
+        acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      for (int q0 = 0; q0 < a.splits; q0 += 4) {
+        float4 v[4][4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            v[q][j] = (on[j] && q0 + q < a.splits)
+                          ? __ldcg(reinterpret_cast<const float4*>(a.partials + (q0 + q) * sstride + off[j]))
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            acc[j].x += v[q][j].x;
+            acc[j].y += v[q][j].y;
+            acc[j].z += v[q][j].z;
+            acc[j].w += v[q][j].w;
+          }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (on[j]) {
+          uint2 w;
+          w.x = sm100::pack_bf16x2(acc[j].x, acc[j].y);
+          w.y = sm100::pack_bf16x2(acc[j].z, acc[j].w);
+          *reinterpret_cast<uint2*>(a.out + off[j]) = w;
+        }
     }
   }
   if (threadIdx.x == 0) a.counters[b] = 0;
@@ -226,7 +266,7 @@ int skinny_splits(int64_t N, int64_t K, int sms) {
   const int64_t kblocks = (K + SBK - 1) / SBK;
   int64_t s = std::max<int64_t>(1, sms / nblocks);
   s = std::min<int64_t>(s, std::max<int64_t>(1, kblocks / 2));  // at least two K blocks per split
-  return static_cast<int>(std::min<int64_t>(s, 32));
+  return static_cast<int>(std::min<int64_t>(s, 16));
 }
 
 void gemm_skinny(const void* x, const void* w, void* out, float* partials, unsigned* counters, int64_t M, int64_t N,
