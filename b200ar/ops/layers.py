@@ -1,0 +1,101 @@
+"""Decoder layer ops on the hand-written sm_100a kernels (``csrc/model``),
+each with a plain-PyTorch fp32 reference used by the tests.
+
+* ``rmsnorm``            y = x * rsqrt(mean(x^2) + eps) * gamma
+* ``RotaryTable``        cos/sin tables for RoPE (theta, head_dim, max positions)
+* ``rope_kv``            rotate q and k (rotate-half convention), write k and v into the KV cache
+* ``decode_attention``   GQA decode attention over the KV cache (split-KV, online softmax)
+* ``silu_mul``           silu(gate) * up
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Dict, Tuple
+
+import torch
+
+from .._native import _C
+
+
+def rmsnorm(x: torch.Tensor, gamma: torch.Tensor, eps: float = 1e-5, out=None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty_like(x)
+    _C.rmsnorm(x.contiguous(), gamma, out, float(eps))
+    return out
+
+
+def ref_rmsnorm(x, gamma, eps=1e-5):
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * gamma.float()).to(x.dtype)
+
+
+class RotaryTable:
+    """cos/sin of position * theta^(-2i/d) for i < d/2, fp32 on the device."""
+
+    def __init__(self, head_dim: int, max_pos: int, theta: float, device):
+        inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+        ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
+        self.cos = ang.cos().float().to(device).contiguous()
+        self.sin = ang.sin().float().to(device).contiguous()
+        self.head_dim = head_dim
+
+
+def rope_kv(qkv, pos, rot: RotaryTable, q_out, k_cache, v_cache, hq: int, hkv: int) -> None:
+    """qkv [B, (hq + 2 hkv) * d] -> q_out [B, hq, d]; k, v into caches [B, L, hkv, d] at ``pos``."""
+    _C.rope_kv(qkv, pos, rot.cos, rot.sin, q_out, k_cache, v_cache, hq, hkv, rot.head_dim)
+
+
+def ref_rope(x, pos, rot: RotaryTable):
+    """x [B, H, d] fp32 reference of the rotate-half rotation."""
+    half = x.shape[-1] // 2
+    c = rot.cos[pos.long()][:, None, :]
+    s = rot.sin[pos.long()][:, None, :]
+    x0, x1 = x[..., :half].float(), x[..., half:].float()
+    return torch.cat([x0 * c - x1 * s, x1 * c + x0 * s], dim=-1)
+
+
+_ATTN_WS: Dict[Tuple[int, int], Tuple[torch.Tensor, torch.Tensor]] = {}
+
+
+def decode_attention(q, k_cache, v_cache, seq_len, hq: int, hkv: int, out=None, splits: int = 0):
+    """q [B, hq, 128]; caches [B, L, hkv, 128]; seq_len int32 [B] -> out [B, hq * 128]."""
+    b = q.shape[0]
+    if out is None:
+        out = torch.empty(b, hq * 128, dtype=q.dtype, device=q.device)
+    if splits <= 0:
+        splits = _C.attention_splits(b, hkv, k_cache.shape[1])
+    key = (q.device.index or 0, b * hq * splits)
+    if key not in _ATTN_WS:
+        _ATTN_WS[key] = (torch.empty(b * hq * splits * 128, dtype=torch.float32, device=q.device),
+                         torch.empty(b * hq * splits * 2, dtype=torch.float32, device=q.device))
+    acc, ml = _ATTN_WS[key]
+    _C.decode_attention(q, k_cache, v_cache, seq_len, out, acc, ml, hq, hkv, splits, 1.0 / math.sqrt(128))
+    return out
+
+
+def ref_decode_attention(q, k_cache, v_cache, seq_len, hq: int, hkv: int):
+    b = q.shape[0]
+    g = hq // hkv
+    out = torch.empty(b, hq, 128, dtype=torch.float32, device=q.device)
+    for i in range(b):
+        n = int(seq_len[i])
+        k = k_cache[i, :n].float().repeat_interleave(g, dim=1)  # [n, hq, d]
+        v = v_cache[i, :n].float().repeat_interleave(g, dim=1)
+        sc = torch.einsum("hd,nhd->hn", q[i].float(), k) / math.sqrt(128)
+        p = torch.softmax(sc, dim=-1)
+        out[i] = torch.einsum("hn,nhd->hd", p, v)
+    return out.reshape(b, hq * 128)
+
+
+def silu_mul(gate_up, out=None):
+    rows, two_i = gate_up.shape
+    if out is None:
+        out = torch.empty(rows, two_i // 2, dtype=gate_up.dtype, device=gate_up.device)
+    _C.silu_mul(gate_up, out)
+    return out
+
+
+def ref_silu_mul(gate_up):
+    g, u = gate_up.float().chunk(2, dim=-1)
+    return (torch.nn.functional.silu(g) * u).to(gate_up.dtype)

@@ -6,6 +6,7 @@
 #include <torch/extension.h>
 
 #include "../gemm/gemm_api.h"
+#include "../model/model.h"
 
 namespace py = pybind11;
 
@@ -33,6 +34,46 @@ void register_ops(py::module& m) {
       },
       "C = A @ B^T with the tcgen05 GEMM (bf16 in/out, fp32 accumulate)", py::arg("a"), py::arg("b"), py::arg("c"),
       py::arg("err"), py::arg("max_ctas") = 0);
+  auto stream = []() { return at::cuda::getCurrentCUDAStream().stream(); };
+  m.def(
+      "rmsnorm",
+      [stream](const at::Tensor& x, const at::Tensor& gamma, at::Tensor& y, double eps) {
+        TORCH_CHECK(x.is_contiguous() && y.is_contiguous() && x.scalar_type() == at::kBFloat16, "bf16 contiguous");
+        const at::cuda::OptionalCUDAGuard guard(device_of(x));
+        b200ar::rmsnorm(x.data_ptr(), gamma.data_ptr(), y.data_ptr(), x.numel() / gamma.numel(), gamma.numel(),
+                        static_cast<float>(eps), stream());
+      },
+      py::arg("x"), py::arg("gamma"), py::arg("y"), py::arg("eps"));
+  m.def(
+      "rope_kv",
+      [stream](const at::Tensor& qkv, const at::Tensor& pos, const at::Tensor& cos_t, const at::Tensor& sin_t,
+               at::Tensor& q_out, at::Tensor& k_cache, at::Tensor& v_cache, int hq, int hkv, int head_dim) {
+        TORCH_CHECK(pos.scalar_type() == at::kInt && cos_t.scalar_type() == at::kFloat, "pos int32, tables fp32");
+        TORCH_CHECK(k_cache.dim() == 4, "KV cache is [batch, max_len, kv_heads, head_dim]");
+        const at::cuda::OptionalCUDAGuard guard(device_of(qkv));
+        b200ar::rope_kv(qkv.data_ptr(), pos.data_ptr<int>(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
+                        q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), qkv.size(0), hq, hkv, head_dim,
+                        static_cast<int>(k_cache.size(1)), stream());
+      });
+  m.def("attention_splits", &b200ar::attention_splits);
+  m.def(
+      "decode_attention",
+      [stream](const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache, const at::Tensor& seq_len,
+               at::Tensor& out, at::Tensor& part_acc, at::Tensor& part_ml, int hq, int hkv, int splits, double scale) {
+        const int64_t b = q.size(0);
+        TORCH_CHECK(part_acc.numel() >= b * hq * splits * 128 && part_ml.numel() >= b * hq * splits * 2,
+                    "attention workspace too small");
+        const at::cuda::OptionalCUDAGuard guard(device_of(q));
+        b200ar::decode_attention(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), seq_len.data_ptr<int>(),
+                                 out.data_ptr(), part_acc.data_ptr<float>(), part_ml.data_ptr<float>(), b, hq, hkv,
+                                 128, static_cast<int>(k_cache.size(1)), splits, static_cast<float>(scale), stream());
+      });
+  m.def(
+      "silu_mul",
+      [stream](const at::Tensor& gu, at::Tensor& y) {
+        const at::cuda::OptionalCUDAGuard guard(device_of(gu));
+        b200ar::silu_mul(gu.data_ptr(), y.data_ptr(), gu.size(0), y.size(1), stream());
+      });
   m.def("skinny_splits", &b200ar::skinny_splits, py::arg("n"), py::arg("k"), py::arg("sms"));
   m.def(
       "gemm_skinny",

@@ -1,0 +1,58 @@
+"""Decoder model kernels against plain-PyTorch fp32 references."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a GPU", allow_module_level=True)
+
+
+@pytest.mark.parametrize("rows,hidden", [(1, 8192), (33, 8192), (4, 4096), (7, 1024)])
+def test_rmsnorm(rows, hidden):
+    from b200ar.ops.layers import ref_rmsnorm, rmsnorm
+
+    x = torch.randn(rows, hidden, device="cuda").to(torch.bfloat16)
+    g = (1 + 0.01 * torch.randn(hidden, device="cuda")).to(torch.bfloat16)
+    torch.testing.assert_close(rmsnorm(x, g).float(), ref_rmsnorm(x, g).float(), atol=2e-2, rtol=1e-2)
+
+
+def test_rope_kv_writes_cache():
+    from b200ar.ops.layers import RotaryTable, ref_rope, rope_kv
+
+    b, hq, hkv, d, L = 3, 8, 1, 128, 64
+    rot = RotaryTable(d, 4096, 500000.0, "cuda")
+    qkv = torch.randn(b, (hq + 2 * hkv) * d, device="cuda").to(torch.bfloat16)
+    pos = torch.tensor([0, 5, 63], dtype=torch.int32, device="cuda")
+    q = torch.empty(b, hq, d, dtype=torch.bfloat16, device="cuda")
+    kc = torch.zeros(b, L, hkv, d, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    rope_kv(qkv, pos, rot, q, kc, vc, hq, hkv)
+    x = qkv.view(b, hq + 2 * hkv, d)
+    torch.testing.assert_close(q.float(), ref_rope(x[:, :hq], pos, rot), atol=2e-2, rtol=1e-2)
+    for i in range(b):
+        p = int(pos[i])
+        torch.testing.assert_close(kc[i, p].float(), ref_rope(x[i:i + 1, hq:hq + hkv], pos[i:i + 1], rot)[0],
+                                   atol=2e-2, rtol=1e-2)
+        assert torch.equal(vc[i, p], x[i, hq + hkv:])
+
+
+@pytest.mark.parametrize("b,hq,hkv,L", [(1, 8, 1, 2049), (8, 8, 1, 2049), (4, 8, 2, 300), (2, 4, 4, 100)])
+def test_decode_attention(b, hq, hkv, L):
+    from b200ar.ops.layers import decode_attention, ref_decode_attention
+
+    q = torch.randn(b, hq, 128, device="cuda").to(torch.bfloat16)
+    kc = torch.randn(b, L + 16, hkv, 128, device="cuda").to(torch.bfloat16)
+    vc = torch.randn(b, L + 16, hkv, 128, device="cuda").to(torch.bfloat16)
+    seq = torch.tensor([L - (i % 3) for i in range(b)], dtype=torch.int32, device="cuda")
+    out = decode_attention(q, kc, vc, seq, hq, hkv)
+    ref = ref_decode_attention(q, kc, vc, seq, hq, hkv)
+    torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
+
+
+def test_silu_mul():
+    from b200ar.ops.layers import ref_silu_mul, silu_mul
+
+    gu = torch.randn(5, 2 * 3584, device="cuda").to(torch.bfloat16)
+    torch.testing.assert_close(silu_mul(gu).float(), ref_silu_mul(gu).float(), atol=2e-2, rtol=1e-2)
