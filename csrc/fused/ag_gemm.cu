@@ -131,10 +131,10 @@ void ag_gemm(Communicator& comm, cudaStream_t stream, const void* x_shard, const
   static bool attr = false;
   if (!attr) {
     B200AR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(gemm::SMEM_BYTES)));
+                                     static_cast<int>(gemm::smem_bytes<gemm::StoreC>())));
     attr = true;
   }
-  kern<<<gemm_grid(s, 0), gemm::THREADS, gemm::SMEM_BYTES, stream>>>(ga, tb, s, epi, err);
+  kern<<<gemm_grid(s, 0), gemm::THREADS, gemm::smem_bytes<gemm::StoreC>(), stream>>>(ga, tb, s, epi, err);
   B200AR_CUDA(cudaGetLastError());
   comm.count_launch();
 }

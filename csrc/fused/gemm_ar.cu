@@ -59,19 +59,41 @@ struct ArEpi {
     return read_generation(ctx, &s_gen);
   }
 
-  // 32 columns of one row of tile (tm, tn): bf16 straight into the owner's inbox.
+  // Each epilogue warp stages its 32 rows x 128 columns (bf16) in shared
+  // memory, then copies them to the owner's inbox two rows (2 x 256 bytes
+  // contiguous) per store instruction, so the P2P writes go out as long runs.
+  // Row stride 256 bytes; 16-byte chunk j of row r is stored at chunk j ^ (r & 15)
+  // so that the row-wise writes and the chunk-wise reads avoid bank conflicts.
+  static constexpr int kStageRow = 128 * 2;
+  static constexpr size_t kStageBytes = 4 * 32 * kStageRow;
+
   __device__ __forceinline__ void store(const gemm::Shape& s, int row, int col, const float* v, int tm, int tn,
-                                        uint32_t gen) const {
-    const int t = tn * s.tiles_m + tm;
-    const int owner = t % world;
-    const int lr = row - tm * gemm::BM;
-    const int lc = col - tn * gemm::BN;
-    char* dst = inbox(gen, owner, ctx.rank, t / world) + (static_cast<int64_t>(lr) * gemm::BN + lc) * 2;
+                                        uint32_t gen, uint8_t* smem) const {
+    const int warp = (threadIdx.x >> 5) & 3, lane = threadIdx.x & 31;
+    const int lc = col - tn * gemm::BN;  // 0, 32, ..., 224
+    uint8_t* stage = smem + warp * 32 * kStageRow;
     uint32_t w[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) w[i] = sm100::pack_bf16x2(v[2 * i], v[2 * i + 1]);
+    uint8_t* mine = stage + lane * kStageRow;
+    const int chunk0 = (lc % 128) / 8;  // first logical 16-byte chunk of these 32 columns
 #pragma unroll
-    for (int i = 0; i < 4; ++i) st_cg(dst + 16 * i, make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]));
+    for (int i = 0; i < 4; ++i)
+      *reinterpret_cast<uint4*>(mine + (((chunk0 + i) ^ (lane & 15)) * 16)) =
+          make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    if (lc % 128 != 96) return;
+    __syncwarp();
+    const int t = tn * s.tiles_m + tm;
+    const int lr0 = row - lane - tm * gemm::BM;  // first row of this warp within the tile
+    char* dst = inbox(gen, t % world, ctx.rank, t / world) +
+                (static_cast<int64_t>(lr0) * gemm::BN + (lc / 128) * 128) * 2;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int r = 2 * i + (lane >> 4), c16 = lane & 15;
+      const uint4 val = *reinterpret_cast<const uint4*>(stage + r * kStageRow + ((c16 ^ (r & 15)) * 16));
+      st_cg(dst + static_cast<int64_t>(r) * gemm::BN * 2 + c16 * 16, val);
+    }
+    __syncwarp();
   }
 
   // After the 4 epilogue warps stored the tile (named barrier in the caller).
@@ -182,7 +204,7 @@ void gemm_allreduce(Communicator& comm, cudaStream_t stream, const void* A, cons
   static bool attr = false;
   if (!attr) {
     B200AR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(gemm::SMEM_BYTES)));
+                                     static_cast<int>(gemm::smem_bytes<ArEpi>())));
     attr = true;
   }
   // Every CTA must be resident (ranks wait on each other's CTAs): one per SM.
@@ -190,7 +212,7 @@ void gemm_allreduce(Communicator& comm, cudaStream_t stream, const void* A, cons
   B200AR_CUDA(cudaGetDevice(&dev));
   B200AR_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int grid = std::max(1, std::min(sms, kMaxCTAs));
-  kern<<<grid, gemm::THREADS, gemm::SMEM_BYTES, stream>>>(ta, tb, s, epi, err);
+  kern<<<grid, gemm::THREADS, gemm::smem_bytes<ArEpi>(), stream>>>(ta, tb, s, epi, err);
   B200AR_CUDA(cudaGetLastError());
   comm.count_launch();
 }

@@ -91,10 +91,10 @@ void gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int6
   static bool attr = false;
   if (!attr) {
     B200AR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(gemm::SMEM_BYTES)));
+                                     static_cast<int>(gemm::smem_bytes<gemm::StoreC>())));
     attr = true;
   }
-  kern<<<gemm_grid(s, max_ctas), gemm::THREADS, gemm::SMEM_BYTES, stream>>>(ta, tb, s, epi, err);
+  kern<<<gemm_grid(s, max_ctas), gemm::THREADS, gemm::smem_bytes<gemm::StoreC>(), stream>>>(ta, tb, s, epi, err);
   B200AR_CUDA(cudaGetLastError());
 }
 

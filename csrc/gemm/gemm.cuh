@@ -28,6 +28,12 @@ constexpr uint32_t A_BYTES = BM * BK * 2;  // 16 KB
 constexpr uint32_t B_BYTES = BN * BK * 2;  // 32 KB
 constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr size_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+// Dynamic shared memory of a kernel instance: ring + barriers + the
+// epilogue's staging area (Epi::kStageBytes, 0 for direct stores).
+template <class Epi>
+constexpr size_t smem_bytes() {
+  return SMEM_BYTES + Epi::kStageBytes;
+}
 constexpr uint32_t TMEM_COLS = 2 * BN;
 
 enum GemmError : int { kGemmOk = 0, kGemmTimeout = 1 };
@@ -42,8 +48,9 @@ struct StoreC {
   __nv_bfloat16* c;
   int64_t ldc;
   // Writes 32 consecutive columns [col, col + 32) of `row` (fp32 values v).
-  __device__ __forceinline__ void store(const Shape& s, int row, int col, const float* v, int, int,
-                                        uint32_t) const {
+  static constexpr size_t kStageBytes = 0;
+  __device__ __forceinline__ void store(const Shape& s, int row, int col, const float* v, int, int, uint32_t,
+                                        uint8_t*) const {
     if (row >= s.M) return;
     uint32_t w[16];
 #pragma unroll
@@ -93,6 +100,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* tempty = tfull + 2;       // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* s_err = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* epi_smem = smem + STAGES * STAGE_BYTES + 256;  // Epi::kStageBytes, 16-byte aligned
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -210,7 +218,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         sm100::tmem_ld_32x32b_x32(taddr + c, r);
         sm100::tmem_ld_wait();
         const int col = tn * BN + c;
-        if (col < s.N) epi.store(s, row, col, reinterpret_cast<const float*>(r), tm, tn, hook);
+        if (col < s.N || Epi::kStageBytes) epi.store(s, row, col, reinterpret_cast<const float*>(r), tm, tn, hook, epi_smem);
       }
       sm100::tc_fence_before();
       __syncwarp();

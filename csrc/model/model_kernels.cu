@@ -129,25 +129,43 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
     l[g] = 0.f;
     acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
   }
-  for (int t = t0 + warp; t < t1; t += kAttnWarps) {
-    const int64_t off = ((static_cast<int64_t>(b) * max_len + t) * hkv + kh) * kHeadDim + lane * 4;
-    const uint2 kr = __ldg(reinterpret_cast<const uint2*>(k_cache + off));
-    const uint2 vr = __ldg(reinterpret_cast<const uint2*>(v_cache + off));
-    const float kx[4] = {__uint_as_float(kr.x << 16), __uint_as_float(kr.x & 0xffff0000u),
-                         __uint_as_float(kr.y << 16), __uint_as_float(kr.y & 0xffff0000u)};
-    const float vx[4] = {__uint_as_float(vr.x << 16), __uint_as_float(vr.x & 0xffff0000u),
-                         __uint_as_float(vr.y << 16), __uint_as_float(vr.y & 0xffff0000u)};
+  // Each warp takes kUnroll consecutive tokens per step: their K/V loads are
+  // issued together, then scored one after the other (hides load latency).
+  constexpr int kUnroll = 4;
+  for (int tb = t0 + warp * kUnroll; tb < t1; tb += kAttnWarps * kUnroll) {
+    uint2 kr[kUnroll], vr[kUnroll];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float sc = qv[g][0] * kx[0] + qv[g][1] * kx[1] + qv[g][2] * kx[2] + qv[g][3] * kx[3];
-      sc = warp_sum(sc);
-      const float mn = fmaxf(m[g], sc);
-      const float corr = __expf(m[g] - mn);
-      const float pexp = __expf(sc - mn);
-      l[g] = l[g] * corr + pexp;
+    for (int u = 0; u < kUnroll; ++u) {
+      const int t = tb + u < t1 ? tb + u : t1 - 1;
+      const int64_t off = ((static_cast<int64_t>(b) * max_len + t) * hkv + kh) * kHeadDim + lane * 4;
+      kr[u] = __ldg(reinterpret_cast<const uint2*>(k_cache + off));
+      vr[u] = __ldg(reinterpret_cast<const uint2*>(v_cache + off));
+    }
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[g][e] = acc[g][e] * corr + pexp * vx[e];
-      m[g] = mn;
+    for (int u = 0; u < kUnroll; ++u) {
+      if (tb + u >= t1) break;
+      const float kx[4] = {__uint_as_float(kr[u].x << 16), __uint_as_float(kr[u].x & 0xffff0000u),
+                           __uint_as_float(kr[u].y << 16), __uint_as_float(kr[u].y & 0xffff0000u)};
+      const float vx[4] = {__uint_as_float(vr[u].x << 16), __uint_as_float(vr[u].x & 0xffff0000u),
+                           __uint_as_float(vr[u].y << 16), __uint_as_float(vr[u].y & 0xffff0000u)};
+      float sc[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) sc[g] = qv[g][0] * kx[0] + qv[g][1] * kx[1] + qv[g][2] * kx[2] + qv[g][3] * kx[3];
+      // All G reductions interleaved (independent shuffle chains).
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int g = 0; g < G; ++g) sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], o);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float mn = fmaxf(m[g], sc[g]);
+        const float corr = __expf(m[g] - mn);
+        const float pexp = __expf(sc[g] - mn);
+        l[g] = l[g] * corr + pexp;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[g][e] = acc[g][e] * corr + pexp * vx[e];
+        m[g] = mn;
+      }
     }
   }
   // Merge the 4 warps through shared memory.
