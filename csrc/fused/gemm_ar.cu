@@ -133,15 +133,37 @@ struct ArEpi {
       if (s_fail) break;
       const int tm = t % s.tiles_m, tn = t / s.tiles_m;
       char* ob = outbox(gen, r, ti);
-      for (int64_t p = threadIdx.x; p < kTileBytes / 16; p += blockDim.x) {
-        float acc[8];
-        unpack_set<__nv_bfloat16>(ld_cg(inbox(gen, r, 0, ti) + p * 16), acc);
-        for (int q = 1; q < world; ++q) unpack_add<__nv_bfloat16>(ld_cg(inbox(gen, r, q, ti) + p * 16), acc);
-        const uint4 v = pack<__nv_bfloat16>(acc);
-        st_cg(ob + p * 16, v);
-        const int lr = static_cast<int>(p / (gemm::BN / 8)), lc = static_cast<int>(p % (gemm::BN / 8)) * 8;
-        const int row = tm * gemm::BM + lr, col = tn * gemm::BN + lc;
-        if (row < s.M && col < s.N) st_out(out + static_cast<int64_t>(row) * s.N + col, v);
+      constexpr int kPk = static_cast<int>(kTileBytes / 16);
+      constexpr int U = 4;  // packets in flight per thread
+      for (int p0 = threadIdx.x; p0 < kPk; p0 += U * blockDim.x) {
+        float acc[U][8];
+        uint4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int p = p0 + u * blockDim.x;
+          v[u] = p < kPk ? ld_cg(inbox(gen, r, 0, ti) + static_cast<int64_t>(p) * 16) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) unpack_set<__nv_bfloat16>(v[u], acc[u]);
+        for (int q = 1; q < world; ++q) {
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int p = p0 + u * blockDim.x;
+            v[u] = p < kPk ? ld_cg(inbox(gen, r, q, ti) + static_cast<int64_t>(p) * 16) : make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int u = 0; u < U; ++u) unpack_add<__nv_bfloat16>(v[u], acc[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int p = p0 + u * blockDim.x;
+          if (p >= kPk) continue;
+          const uint4 o = pack<__nv_bfloat16>(acc[u]);
+          st_cg(ob + static_cast<int64_t>(p) * 16, o);
+          const int lr = p / (gemm::BN / 8), lc = (p % (gemm::BN / 8)) * 8;
+          const int row = tm * gemm::BM + lr, col = tn * gemm::BN + lc;
+          if (row < s.M && col < s.N) st_out(out + static_cast<int64_t>(row) * s.N + col, o);
+        }
       }
       __syncthreads();
       if (threadIdx.x == 0) st_release_sys(&ctx.self->tile_ready[t], epoch);
@@ -156,10 +178,22 @@ struct ArEpi {
         if (s_fail) break;
         const int tm = t % s.tiles_m, tn = t / s.tiles_m;
         const char* ob = outbox(gen, owner, t / world);
-        for (int64_t p = threadIdx.x; p < kTileBytes / 16; p += blockDim.x) {
-          const int lr = static_cast<int>(p / (gemm::BN / 8)), lc = static_cast<int>(p % (gemm::BN / 8)) * 8;
-          const int row = tm * gemm::BM + lr, col = tn * gemm::BN + lc;
-          if (row < s.M && col < s.N) st_out(out + static_cast<int64_t>(row) * s.N + col, ld_cg(ob + p * 16));
+        constexpr int kPk = static_cast<int>(kTileBytes / 16);
+        constexpr int U = 8;  // remote loads in flight per thread
+        for (int p0 = threadIdx.x; p0 < kPk; p0 += U * blockDim.x) {
+          uint4 v[U];
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int p = p0 + u * blockDim.x;
+            v[u] = p < kPk ? ld_cg(ob + static_cast<int64_t>(p) * 16) : make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int p = p0 + u * blockDim.x;
+            const int lr = p / (gemm::BN / 8), lc = (p % (gemm::BN / 8)) * 8;
+            const int row = tm * gemm::BM + lr, col = tn * gemm::BN + lc;
+            if (p < kPk && row < s.M && col < s.N) st_out(out + static_cast<int64_t>(row) * s.N + col, v[u]);
+          }
         }
         __syncthreads();
       }
