@@ -214,6 +214,10 @@ class CustomAllreduce:
         m, n = x.shape[0], w.shape[0]
         if out is None:
             out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+        # Below ~512 rows the 128x256 tiles leave most SMs idle; the split-K
+        # decode GEMM followed by the (Lamport) all-reduce is faster there.
+        if fused and m < 512:
+            fused = False
         if fused and self._comm is not None and self.world > 1 and self._comm.gemm_ar_supported(m, n):
             self._comm.gemm_allreduce(x.contiguous(), w, out, error_word(x.device))
             return out

@@ -275,7 +275,7 @@ def test_nvls_multimem():
 
 def _gemm_allreduce(rank, world):
     # BASELINE config 4 (down projection): x [M, 3584] ~ N(0,1), W [8192, 3584] ~ N(0, 0.02).
-    from b200ar.ops.gemm import check_errors
+    from b200ar.ops.gemm import check_errors, error_word
 
     comm = _comm(rank, max_size=160 << 20)
     K, N = 3584, 8192
@@ -286,12 +286,16 @@ def _gemm_allreduce(rank, world):
         part = (x.float() @ w.float().t())
         ref = part.clone()
         dist.all_reduce(ref)
-        for _ in range(3):
-            out = comm.linear_all_reduce(x, w)
-            torch.cuda.synchronize()
-            check_errors()
-            err = (out.float() - ref).abs().max().item()
-            assert err <= 2e-2 * ref.abs().max().item() + 2e-2, (M, err)
+        for fused in (True, False):
+            for _ in range(2):
+                out = comm.linear_all_reduce(x, w, fused=fused) if not fused else torch.empty_like(ref).to(
+                    torch.bfloat16)
+                if fused:
+                    comm._comm.gemm_allreduce(x, w, out, error_word(x.device))
+                torch.cuda.synchronize()
+                check_errors()
+                err = (out.float() - ref).abs().max().item()
+                assert err <= 2e-2 * ref.abs().max().item() + 2e-2, (M, fused, err)
         outs = [torch.empty_like(out) for _ in range(world)]
         dist.all_gather(outs, out)
         assert all(torch.equal(o, outs[0]) for o in outs), "ranks disagree"
