@@ -117,16 +117,36 @@ __global__ void __launch_bounds__(kArThreads) nvls_kernel(NvlsArgs a) {
     *b = pb + part_begin(len, G, j);
     *e = pb + part_begin(len, G, j + 1);
   };
+  // U packets in flight per thread in every phase (the switch round trip of
+  // multimem.ld_reduce is long; one outstanding request per thread starves it).
+  constexpr int U = 4;
+  const int64_t step = static_cast<int64_t>(U) * blockDim.x;
   int64_t b, e;
 #pragma unroll 1
   for (int p = 0; p < N; ++p) {
     range(p, &b, &e);
-    for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) st_cg(a.uc + i * 16, ld_in(a.in + i * 16));
+    for (int64_t i0 = b + threadIdx.x; i0 < e; i0 += step) {
+      uint4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (i0 + u * blockDim.x < e) v[u] = ld_in(a.in + (i0 + u * blockDim.x) * 16);
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (i0 + u * blockDim.x < e) st_cg(a.uc + (i0 + u * blockDim.x) * 16, v[u]);
+    }
   }
   bool ok = cta_barrier<N>(a.ctx, j, epoch_of(gen, 0));
   if (ok) {
     range(r, &b, &e);
-    for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) mm_st(a.mc + i * 16, mm_ld_reduce<T>(a.mc + i * 16));
+    for (int64_t i0 = b + threadIdx.x; i0 < e; i0 += step) {
+      uint4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (i0 + u * blockDim.x < e) v[u] = mm_ld_reduce<T>(a.mc + (i0 + u * blockDim.x) * 16);
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (i0 + u * blockDim.x < e) mm_st(a.mc + (i0 + u * blockDim.x) * 16, v[u]);
+    }
     __threadfence_system();
   }
   ok = cta_barrier<N>(a.ctx, j, epoch_of(gen, 1)) && ok;
@@ -134,7 +154,15 @@ __global__ void __launch_bounds__(kArThreads) nvls_kernel(NvlsArgs a) {
 #pragma unroll 1
     for (int p = 0; p < N; ++p) {
       range(p, &b, &e);
-      for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) st_out(a.out + i * 16, ld_cg(a.uc + i * 16));
+      for (int64_t i0 = b + threadIdx.x; i0 < e; i0 += step) {
+        uint4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (i0 + u * blockDim.x < e) v[u] = ld_cg(a.uc + (i0 + u * blockDim.x) * 16);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (i0 + u * blockDim.x < e) st_out(a.out + (i0 + u * blockDim.x) * 16, v[u]);
+      }
     }
   }
   finish_generation(a.ctx, gen);
