@@ -103,6 +103,7 @@ class Communicator {
   // marker. Every rank must finish this before any rank uses kLamport.
   void register_lamport(const std::vector<int64_t>& ptrs, int64_t cap);
   int64_t lamport_capacity() const { return lam_cap_; }
+  char* lamport_ptr(int r) const { return lam_[r]; }
 
   // Registers a static user buffer: ptrs[i] = rank i's copy (already mapped).
   void register_buffer(const std::vector<int64_t>& ptrs);

@@ -41,6 +41,8 @@ struct NormArgs {
   int hp;             // H / 8 packets per row
   float eps;
   float inv_h;
+  char* lam[kMaxRanks];  // Lamport regions (barrier-free variant)
+  int64_t lam_cap;
 };
 
 // Sum over the CTA; every thread gets the result.
@@ -135,6 +137,76 @@ __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_oneshot_kernel(Norm
   finish_generation(a.ctx, gen);
 }
 
+// Barrier-free one-shot: partial rows go straight into every rank's current
+// Lamport buffer (markers replaced by data); each rank polls its own buffer,
+// reduces, normalises and restores the markers (see oneshot_lamport_kernel).
+template <int N, int PPT>
+__global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_lamport_kernel(NormArgs a) {
+  __shared__ uint32_t s_gen;
+  __shared__ float red[32];
+  __shared__ int s_fail;
+  const uint32_t gen = read_generation(a.ctx, &s_gen);
+  const int r = a.ctx.rank;
+  const int64_t row_bytes = static_cast<int64_t>(a.hp) * 16;
+  const int64_t buf = static_cast<int64_t>(gen % kLamportBuffers) * N * a.lam_cap;
+  char* dst[N];
+  rotate_ptrs<N>(a.lam, r, dst);
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+      const int idx = threadIdx.x + k * blockDim.x;
+      if (idx < a.hp) {
+        uint4 v = ld_in(a.x + (row * a.hp + idx) * 16);
+        v.x = lamport_clean<__nv_bfloat16>(v.x);
+        v.y = lamport_clean<__nv_bfloat16>(v.y);
+        v.z = lamport_clean<__nv_bfloat16>(v.z);
+        v.w = lamport_clean<__nv_bfloat16>(v.w);
+        const int64_t off = buf + static_cast<int64_t>(r) * a.lam_cap + row * row_bytes + static_cast<int64_t>(idx) * 16;
+#pragma unroll
+        for (int p = 0; p < N; ++p) st_cg(dst[p] + off, v);
+      }
+    }
+  }
+  char* mine = a.lam[r] + buf;
+  if (threadIdx.x == 0) s_fail = 0;
+  __syncthreads();
+  const uint4 marker = make_uint4(kLamportMarker, kLamportMarker, kLamportMarker, kLamportMarker);
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    // Wait until every source's packets of this row arrived (bounded).
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+      const int idx = threadIdx.x + k * blockDim.x;
+      if (idx < a.hp) {
+        for (int q = 0; q < N; ++q) {
+          const char* pk = mine + static_cast<int64_t>(q) * a.lam_cap + row * row_bytes + static_cast<int64_t>(idx) * 16;
+          if (!lamport_ready(ld_volatile16(pk))) {
+            const uint64_t start = global_ns();
+            uint32_t spins = 0;
+            while (!lamport_ready(ld_volatile16(pk))) {
+              if ((++spins & 63u) == 0u && global_ns() - start > a.ctx.timeout_ns) {
+                report_status(a.ctx.status, kStatusTimeout, r, q, blockIdx.x, gen, 0);
+                s_fail = 1;
+                break;
+              }
+            }
+          }
+        }
+      }
+    }
+    if (__syncthreads_or(s_fail)) break;
+    reduce_norm_row<N, PPT>(a, mine + row * row_bytes, a.lam_cap, row, a.y, a.z, nullptr, nullptr, red);
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+      const int idx = threadIdx.x + k * blockDim.x;
+      if (idx < a.hp)
+        for (int q = 0; q < N; ++q)
+          st_cg(mine + static_cast<int64_t>(q) * a.lam_cap + row * row_bytes + static_cast<int64_t>(idx) * 16, marker);
+    }
+  }
+  finish_generation(a.ctx, gen);
+}
+
 // Two-shot. Part p = rows [part_begin(T, N, p), part_begin(T, N, p + 1)); with
 // prow = ceil(T / N) rows per part, every slot holds
 //   inbox  [N][prow] rows : rank q's partial rows of this rank's part
@@ -208,25 +280,28 @@ __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_twoshot_kernel(Norm
   finish_generation(a.ctx, gen);
 }
 
+// kind: 0 one-shot push, 1 two-shot, 2 Lamport.
 template <int N, int PPT>
-void launch_n(bool twoshot, int ctas, int threads, const NormArgs& a, cudaStream_t s) {
-  if (twoshot)
+void launch_n(int kind, int ctas, int threads, const NormArgs& a, cudaStream_t s) {
+  if (kind == 1)
     ar_rmsnorm_twoshot_kernel<N, PPT><<<ctas, threads, 0, s>>>(a);
+  else if (kind == 2)
+    ar_rmsnorm_lamport_kernel<N, PPT><<<ctas, threads, 0, s>>>(a);
   else
     ar_rmsnorm_oneshot_kernel<N, PPT><<<ctas, threads, 0, s>>>(a);
 }
 
 template <int PPT>
-void launch_ppt(int world, bool twoshot, int ctas, int threads, const NormArgs& a, cudaStream_t s) {
+void launch_ppt(int world, int kind, int ctas, int threads, const NormArgs& a, cudaStream_t s) {
   switch (world) {
-    case 1: launch_n<1, PPT>(twoshot, ctas, threads, a, s); break;
-    case 2: launch_n<2, PPT>(twoshot, ctas, threads, a, s); break;
-    case 3: launch_n<3, PPT>(twoshot, ctas, threads, a, s); break;
-    case 4: launch_n<4, PPT>(twoshot, ctas, threads, a, s); break;
-    case 5: launch_n<5, PPT>(twoshot, ctas, threads, a, s); break;
-    case 6: launch_n<6, PPT>(twoshot, ctas, threads, a, s); break;
-    case 7: launch_n<7, PPT>(twoshot, ctas, threads, a, s); break;
-    case 8: launch_n<8, PPT>(twoshot, ctas, threads, a, s); break;
+    case 1: launch_n<1, PPT>(kind, ctas, threads, a, s); break;
+    case 2: launch_n<2, PPT>(kind, ctas, threads, a, s); break;
+    case 3: launch_n<3, PPT>(kind, ctas, threads, a, s); break;
+    case 4: launch_n<4, PPT>(kind, ctas, threads, a, s); break;
+    case 5: launch_n<5, PPT>(kind, ctas, threads, a, s); break;
+    case 6: launch_n<6, PPT>(kind, ctas, threads, a, s); break;
+    case 7: launch_n<7, PPT>(kind, ctas, threads, a, s); break;
+    case 8: launch_n<8, PPT>(kind, ctas, threads, a, s); break;
     default: throw std::invalid_argument("unsupported world size");
   }
 }
@@ -249,22 +324,29 @@ int ar_rmsnorm(Communicator& comm, cudaStream_t stream, const void* x, const voi
   for (const void* p : {x, residual, gamma, static_cast<const void*>(y), static_cast<const void*>(residual_out)})
     B200AR_CHECK(reinterpret_cast<uintptr_t>(p) % 16 == 0, "fused all-reduce + RMSNorm needs 16-byte aligned tensors");
   const int world = comm.world();
+  const int64_t bytes = rows * hidden * 2;
   if (variant == kAuto) {
-    // One-shot moves (N-1) rows per row and needs no second barrier; two-shot
-    // moves 2(N-1)/N and wins once the message is bandwidth bound.
-    const int64_t bytes = rows * hidden * 2;
-    variant = (world <= 2 || bytes <= (512 << 10) || rows < 2 * world) ? kOneshotPush : kTwoshot;
+    // Lamport (no barrier) while the rows fit its buffers; then one-shot push
+    // for small messages; two-shot once the message is bandwidth bound.
+    if (world > 1 && comm.lamport_capacity() >= bytes)
+      variant = kLamport;
+    else
+      variant = (world <= 2 || bytes <= (512 << 10) || rows < 2 * world) ? kOneshotPush : kTwoshot;
   }
-  B200AR_CHECK(variant == kOneshotPush || variant == kTwoshot, "fused RMSNorm supports oneshot_push and twoshot");
+  B200AR_CHECK(variant == kOneshotPush || variant == kTwoshot || variant == kLamport,
+               "fused RMSNorm supports oneshot_push, twoshot and lamport");
   if (world == 1) variant = kOneshotPush;
+  if (variant == kLamport && comm.lamport_capacity() < bytes) variant = kOneshotPush;
   B200AR_CHECK(comm.slots_registered(), "communicator has no slot buffers");
-  const int64_t need = ar_rmsnorm_slot_bytes(variant, rows, hidden, world);
-  if (need > comm.slot_capacity()) {
-    const int other = variant == kTwoshot ? kOneshotPush : kTwoshot;
-    B200AR_CHECK(ar_rmsnorm_slot_bytes(other, rows, hidden, world) <= comm.slot_capacity(),
-                 "fused all-reduce + RMSNorm of " << rows << "x" << hidden << " needs " << need
-                                                  << " slot bytes, capacity is " << comm.slot_capacity());
-    variant = other;
+  if (variant != kLamport) {
+    const int64_t need = ar_rmsnorm_slot_bytes(variant, rows, hidden, world);
+    if (need > comm.slot_capacity()) {
+      const int other = variant == kTwoshot ? kOneshotPush : kTwoshot;
+      B200AR_CHECK(ar_rmsnorm_slot_bytes(other, rows, hidden, world) <= comm.slot_capacity(),
+                   "fused all-reduce + RMSNorm of " << rows << "x" << hidden << " needs " << need
+                                                    << " slot bytes, capacity is " << comm.slot_capacity());
+      variant = other;
+    }
   }
 
   NormArgs a{};
@@ -280,16 +362,19 @@ int ar_rmsnorm(Communicator& comm, cudaStream_t stream, const void* x, const voi
   a.hp = static_cast<int>(hidden / 8);
   a.eps = eps;
   a.inv_h = 1.0f / static_cast<float>(hidden);
+  for (int i = 0; i < world; ++i) a.lam[i] = comm.lamport_ptr(i);
+  a.lam_cap = comm.lamport_capacity();
   const int ppt = a.hp <= kMaxRowThreads ? 1 : (a.hp <= 2 * kMaxRowThreads ? 2 : 4);
   const int threads = std::max(32, ((a.hp + ppt - 1) / ppt + 31) / 32 * 32);
   const bool two = variant == kTwoshot;
+  const int kind = two ? 1 : (variant == kLamport ? 2 : 0);
   const int64_t work_rows = two ? (rows + world - 1) / world : rows;
   int grid = ctas > 0 ? ctas : static_cast<int>(std::min<int64_t>(work_rows, 148));
   grid = std::max(1, std::min(grid, kMaxCTAs));
   switch (ppt) {
-    case 1: launch_ppt<1>(world, two, grid, threads, a, stream); break;
-    case 2: launch_ppt<2>(world, two, grid, threads, a, stream); break;
-    default: launch_ppt<4>(world, two, grid, threads, a, stream); break;
+    case 1: launch_ppt<1>(world, kind, grid, threads, a, stream); break;
+    case 2: launch_ppt<2>(world, kind, grid, threads, a, stream); break;
+    default: launch_ppt<4>(world, kind, grid, threads, a, stream); break;
   }
   B200AR_CUDA(cudaGetLastError());
   comm.count_launch();
@@ -391,9 +476,9 @@ extern "C" int b200ar_residual_rmsnorm_noalloc(const void* x, const void* residu
   const int grid = static_cast<int>(std::min<int64_t>(rows, 148));
   try {
     switch (ppt) {
-      case 1: launch_ppt<1>(1, false, grid, threads, a, stream); break;
-      case 2: launch_ppt<2>(1, false, grid, threads, a, stream); break;
-      default: launch_ppt<4>(1, false, grid, threads, a, stream); break;
+      case 1: launch_ppt<1>(1, 0, grid, threads, a, stream); break;
+      case 2: launch_ppt<2>(1, 0, grid, threads, a, stream); break;
+      default: launch_ppt<4>(1, 0, grid, threads, a, stream); break;
     }
   } catch (const std::exception& ex) {
     return noalloc_fail(2, ex.what());

@@ -208,14 +208,18 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_acc, const fl
                                     __nv_bfloat16* __restrict__ out, int splits) {
   const int64_t bh = blockIdx.x;
   const int dmn = threadIdx.x;
+  const float* ml = part_ml + bh * splits * 2;
+  const float* pa = part_acc + bh * splits * kHeadDim + dmn;
   float mm = -INFINITY;
-  for (int s = 0; s < splits; ++s) mm = fmaxf(mm, part_ml[(bh * splits + s) * 2]);
+#pragma unroll 8
+  for (int s = 0; s < splits; ++s) mm = fmaxf(mm, ml[2 * s]);
   float ll = 0.f, aa = 0.f;
+#pragma unroll 8
   for (int s = 0; s < splits; ++s) {
-    const float ms = part_ml[(bh * splits + s) * 2];
+    const float ms = ml[2 * s];
     const float f = ms == -INFINITY ? 0.f : __expf(ms - mm);
-    ll += part_ml[(bh * splits + s) * 2 + 1] * f;
-    aa += part_acc[(bh * splits + s) * kHeadDim + dmn] * f;
+    ll += ml[2 * s + 1] * f;
+    aa += pa[static_cast<int64_t>(s) * kHeadDim] * f;
   }
   out[bh * kHeadDim + dmn] = __float2bfloat16_rn(ll > 0.f ? aa / ll : 0.f);
 }
@@ -261,7 +265,7 @@ void rope_kv(const void* qkv, const int* pos, const float* cos_t, const float* s
 int attention_splits(int64_t batch, int hkv, int max_len) {
   const int64_t ctas = batch * hkv;
   int s = static_cast<int>(std::max<int64_t>(1, 2 * 148 / std::max<int64_t>(ctas, 1)));
-  s = std::min(s, std::max(1, max_len / 64));
+  s = std::min(s, std::max(1, max_len / 128));  // at least ~128 tokens per split
   return std::min(s, 64);
 }
 

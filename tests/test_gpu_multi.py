@@ -224,7 +224,7 @@ def _fused_rmsnorm(rank, world):
         xs = [torch.empty_like(x) for _ in range(world)]
         dist.all_gather(xs, x)
         y_ref, z_ref = ref_ar_residual_rmsnorm(xs, res, gamma, 1e-5)
-        for variant in ("oneshot_push", "twoshot", "auto"):
+        for variant in ("oneshot_push", "twoshot", "lamport", "auto"):
             y, z = comm.all_reduce_residual_rmsnorm(x, res, gamma, 1e-5, variant=variant)
             torch.cuda.synchronize()
             assert torch.equal(z, z_ref), (T, variant)
