@@ -172,23 +172,32 @@ __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_lamport_kernel(Norm
   __syncthreads();
   const uint4 marker = make_uint4(kLamportMarker, kLamportMarker, kLamportMarker, kLamportMarker);
   for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
-    // Wait until every source's packets of this row arrived (bounded).
+    // Wait until every source's packets of this row arrived (bounded). All
+    // packets are loaded first, so the common case costs one round trip.
+    bool ready[PPT][N];
 #pragma unroll
     for (int k = 0; k < PPT; ++k) {
       const int idx = threadIdx.x + k * blockDim.x;
-      if (idx < a.hp) {
-        for (int q = 0; q < N; ++q) {
-          const char* pk = mine + static_cast<int64_t>(q) * a.lam_cap + row * row_bytes + static_cast<int64_t>(idx) * 16;
-          if (!lamport_ready(ld_volatile16(pk))) {
-            const uint64_t start = global_ns();
-            uint32_t spins = 0;
-            while (!lamport_ready(ld_volatile16(pk))) {
-              if ((++spins & 63u) == 0u && global_ns() - start > a.ctx.timeout_ns) {
-                report_status(a.ctx.status, kStatusTimeout, r, q, blockIdx.x, gen, 0);
-                s_fail = 1;
-                break;
-              }
-            }
+#pragma unroll
+      for (int q = 0; q < N; ++q)
+        ready[k][q] = idx >= a.hp ||
+                      lamport_ready(ld_volatile16(mine + static_cast<int64_t>(q) * a.lam_cap + row * row_bytes +
+                                                  static_cast<int64_t>(idx) * 16));
+    }
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+      const int idx = threadIdx.x + k * blockDim.x;
+#pragma unroll
+      for (int q = 0; q < N; ++q) {
+        if (ready[k][q]) continue;
+        const char* pk = mine + static_cast<int64_t>(q) * a.lam_cap + row * row_bytes + static_cast<int64_t>(idx) * 16;
+        const uint64_t start = global_ns();
+        uint32_t spins = 0;
+        while (!lamport_ready(ld_volatile16(pk))) {
+          if ((++spins & 63u) == 0u && global_ns() - start > a.ctx.timeout_ns) {
+            report_status(a.ctx.status, kStatusTimeout, r, q, blockIdx.x, gen, 0);
+            s_fail = 1;
+            break;
           }
         }
       }
