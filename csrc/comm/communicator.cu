@@ -7,6 +7,7 @@
 
 #include "ar_kernels.cuh"
 #include "communicator.h"
+#include "../common/trace.h"
 #include "../nvls/nvls.h"
 
 namespace b200ar {
@@ -288,6 +289,7 @@ LaunchInfo Communicator::plan(int64_t bytes, int variant, int ctas, bool capturi
 
 LaunchInfo Communicator::allreduce(cudaStream_t stream, const void* in, void* out, int64_t bytes, DType dt,
                                    int variant, int ctas) {
+  TraceRange trace("b200ar.all_reduce");
   check_status();
   B200AR_CHECK(bytes % 16 == 0, "all-reduce size must be a multiple of 16 bytes, got " << bytes);
   B200AR_CHECK(reinterpret_cast<uintptr_t>(in) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0,

@@ -16,6 +16,7 @@
 
 #include "../comm/ar_kernels.cuh"
 #include "../comm/communicator.h"
+#include "../common/trace.h"
 #include "../gemm/gemm.cuh"
 #include "../gemm/gemm_api.h"
 #include "fused.h"
@@ -97,6 +98,7 @@ bool ag_gemm_supported(Communicator& comm, int64_t rows_per_rank, int64_t K) {
 
 void ag_gemm(Communicator& comm, cudaStream_t stream, const void* x_shard, const void* W, void* Y,
              int64_t rows_per_rank, int64_t N, int64_t K, int* err) {
+  TraceRange trace("b200ar.ag_gemm");
   comm.check_status();
   B200AR_CHECK(ag_gemm_supported(comm, rows_per_rank, K),
                "all-gather GEMM needs rows per rank a multiple of " << kSliceRows << " and a shard of at most "

@@ -21,6 +21,7 @@
 
 #include "../comm/ar_kernels.cuh"
 #include "../comm/communicator.h"
+#include "../common/trace.h"
 #include "fused.h"
 
 namespace b200ar {
@@ -326,6 +327,7 @@ int64_t ar_rmsnorm_slot_bytes(int variant, int64_t rows, int64_t hidden, int wor
 
 int ar_rmsnorm(Communicator& comm, cudaStream_t stream, const void* x, const void* residual, const void* gamma,
                void* y, void* residual_out, int64_t rows, int64_t hidden, float eps, int variant, int ctas) {
+  TraceRange trace("b200ar.ar_rmsnorm");
   comm.check_status();
   B200AR_CHECK(hidden % 8 == 0 && hidden / 8 <= 4 * kMaxRowThreads,
                "hidden size must be a multiple of 8 and at most " << 32 * kMaxRowThreads);

@@ -26,6 +26,7 @@
 
 #include "../comm/ar_kernels.cuh"
 #include "../comm/communicator.h"
+#include "../common/trace.h"
 #include "../gemm/gemm.cuh"
 #include "../gemm/gemm_api.h"
 #include "fused.h"
@@ -219,6 +220,7 @@ bool gemm_ar_supported(Communicator& comm, int64_t M, int64_t N) {
 
 void gemm_allreduce(Communicator& comm, cudaStream_t stream, const void* A, const void* W, void* out, int64_t M,
                     int64_t N, int64_t K, int* err) {
+  TraceRange trace("b200ar.gemm_allreduce");
   comm.check_status();
   B200AR_CHECK(gemm_ar_supported(comm, M, N),
                "fused GEMM + all-reduce of " << M << "x" << N << " needs at least world tiles, at most " << kMaxTiles

@@ -160,3 +160,37 @@ def _fused_cpu(rank, world):
 
 def test_fused_residual_rmsnorm_cpu():
     run_ranks(_fused_cpu, 2)
+
+
+def _dead_peer(rank, world):
+    # Rank 1 leaves after set-up without ever calling the collective: rank 0's
+    # barrier must end in a CommTimeoutError (bounded wait), not a hang.
+    import time
+
+    from b200ar import CommTimeoutError, CustomAllreduce
+
+    comm = CustomAllreduce(device="cpu", max_size=1 << 20, timeout_ms=300)
+    if rank == 1:
+        return
+    t0 = time.time()
+    with pytest.raises(CommTimeoutError):
+        comm.all_reduce(torch.ones(4096), variant="twoshot")
+    assert time.time() - t0 < 10
+
+
+def test_dead_peer_times_out():
+    import torch.multiprocessing as mp  # noqa: F401
+
+    from dist_util import run_ranks as _run
+
+    # The surviving rank must not wait on a barrier of the process group at exit.
+    _run(_dead_peer_entry, 2)
+
+
+def _dead_peer_entry(rank, world):
+    import torch.distributed as dist
+
+    _dead_peer(rank, world)
+    # Skip the final dist.barrier() of the harness for the departed rank: both
+    # ranks meet here once rank 0 observed the timeout.
+    dist.barrier()

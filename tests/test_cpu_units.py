@@ -1,0 +1,106 @@
+"""CPU unit tests: selector tables, crossover detection, configuration,
+reference-compatible exports and IPC handle serialisation (no GPU needed)."""
+
+import json
+import pickle
+
+import pytest
+
+
+def test_build_table_merges_and_covers_everything():
+    from b200ar.parallel.selector import build_table
+
+    rows = []
+    for size, best in ((4096, "lamport"), (8192, "lamport"), (1 << 20, "twoshot"), (1 << 28, "nccl")):
+        for v in ("lamport", "twoshot", "nccl"):
+            rows.append({"bytes": size, "variant": v, "ctas": 8, "us": 1.0 if v == best else 5.0})
+    table = build_table(rows)
+    assert [e[1] for e in table] == ["lamport", "twoshot", "nccl"]
+    assert table[0][0] == 8192 and table[1][0] == 1 << 20
+    assert table[-1][0] >= 1 << 62  # the last entry covers every larger size
+
+
+def test_crossover_bytes():
+    from b200ar.parallel.selector import crossover_bytes
+
+    rows = []
+    for s, (ours, nccl) in {1: (1, 2), 2: (1, 2), 4: (3, 2), 8: (5, 2)}.items():
+        rows += [{"bytes": s, "impl": "custom", "us": ours}, {"bytes": s, "impl": "nccl", "us": nccl}]
+    assert crossover_bytes(rows) == 4
+    rows = [{"bytes": 1, "impl": "custom", "us": 1}, {"bytes": 1, "impl": "nccl", "us": 2}]
+    assert crossover_bytes(rows) is None
+
+
+def test_load_table_picks_nearest_world(tmp_path):
+    from b200ar.parallel.selector import FALLBACK, load_table, save_tables
+
+    p = tmp_path / "t.json"
+    save_tables(str(p), {2: [(100, "lamport", 1)], 8: [(200, "twoshot", 4)]})
+    assert load_table(2, str(p)) == [(100, "lamport", 1)]
+    assert load_table(6, str(p)) == [(200, "twoshot", 4)]
+    assert load_table(3, str(p)) == [(100, "lamport", 1)]
+    assert load_table(4, str(tmp_path / "missing.json")) == FALLBACK
+    data = json.loads(p.read_text())
+    assert set(data["tables"]) == {"2", "8"}
+
+
+def test_packaged_table_is_valid():
+    from b200ar.parallel.selector import VARIANTS, load_table
+
+    for w in (2, 4, 8):
+        table = load_table(w)
+        assert table and all(v in VARIANTS for _, v, _ in table)
+        sizes = [b for b, _, _ in table]
+        assert sizes == sorted(sizes)
+
+
+def test_variant_ids_roundtrip():
+    from b200ar.parallel.selector import VARIANT_NAMES, VARIANTS, variant_id
+
+    for name, vid in VARIANTS.items():
+        assert variant_id(name) == vid and VARIANT_NAMES[vid] == name
+    with pytest.raises(ValueError):
+        variant_id("nope")
+
+
+def test_config_env_overrides(monkeypatch):
+    from b200ar.config import default_config
+
+    monkeypatch.setenv("B200AR_MAX_SIZE", "1234")
+    monkeypatch.setenv("B200AR_NVLS", "1")
+    cfg = default_config({"timeout_ms": 7})
+    assert cfg.max_size == 1234 and cfg.enable_nvls and cfg.timeout_ms == 7
+
+
+def test_compat_exports_match_reference_api():
+    import b200ar.compat as c
+
+    names = ["init_custom_ar", "all_reduce", "dispose", "meta_size", "register_buffer", "register_pcie_buffers",
+             "get_graph_buffer_ipc_meta", "register_graph_buffers"]
+    assert sorted(c.__all__) == sorted(names)
+    for n in names:
+        assert callable(getattr(c, n))
+    assert c.meta_size() > 0 and c.meta_size() % 256 == 0
+
+
+def test_ipc_handle_pickles():
+    from b200ar.ipc import HANDLE_BYTES, cudaIpcMemHandle_t
+
+    raw = bytes(range(HANDLE_BYTES))
+    h = cudaIpcMemHandle_t.from_bytes(raw)
+    h2 = pickle.loads(pickle.dumps(h))
+    assert h2.to_bytes() == raw
+    with pytest.raises(ValueError):
+        cudaIpcMemHandle_t.from_bytes(b"short")
+
+
+def test_slot_bytes_formulas():
+    from b200ar import _C
+    from b200ar.parallel.selector import VARIANTS
+
+    assert _C.variant_slot_bytes(VARIANTS["oneshot_push"], 1024, 8) == 8192
+    assert _C.variant_slot_bytes(VARIANTS["oneshot_pull"], 1024, 8) == 1024
+    # two-shot: (world + 1) parts of ceil(packets / world) packets
+    assert _C.variant_slot_bytes(VARIANTS["twoshot"], 16 * 10, 4) == 5 * 3 * 16
+    assert _C.lamport_bytes(1024, 8) == 3 * 8 * 1024
+    assert _C.gemm_ar_slot_bytes(128, 256, 2) == 3 * 1 * 128 * 256 * 2
