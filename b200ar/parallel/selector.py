@@ -13,6 +13,7 @@ name ``nccl``: the measured crossover above which NCCL is faster.
 from __future__ import annotations
 
 import json
+import math
 import os
 from typing import Dict, Iterable, List, Optional, Sequence, Tuple
 
@@ -52,8 +53,8 @@ def load_table(world: int, path: Optional[str] = None) -> List[Entry]:
             data = json.load(f)
         tables = {int(k): v for k, v in data.get("tables", {}).items() if v}
         if tables:
-            # Nearest measured world size (ties go to the larger one).
-            best = min(tables, key=lambda w: (abs(w - world), -w))
+            # Nearest measured world size on a log scale (ties go to the larger one).
+            best = min(tables, key=lambda w: (abs(math.log2(w) - math.log2(max(world, 1))), -w))
             return [(int(b), str(v), int(c)) for b, v, c in tables[best]]
     return list(FALLBACK)
 

@@ -39,6 +39,7 @@ def test_load_table_picks_nearest_world(tmp_path):
     assert load_table(2, str(p)) == [(100, "lamport", 1)]
     assert load_table(6, str(p)) == [(200, "twoshot", 4)]
     assert load_table(3, str(p)) == [(100, "lamport", 1)]
+    assert load_table(4, str(p)) == [(200, "twoshot", 4)]  # log-scale tie -> larger world
     assert load_table(4, str(tmp_path / "missing.json")) == FALLBACK
     data = json.loads(p.read_text())
     assert set(data["tables"]) == {"2", "8"}
