@@ -25,7 +25,7 @@ class Config:
     # Largest message (bytes) for which the one-shot push variant is allowed.
     push_max_size: int = dataclasses.field(default_factory=lambda: _env_int("B200AR_PUSH_MAX_SIZE", 1 << 20))
     # Largest message (bytes) for the barrier-free one-shot Lamport variant.
-    lamport_max_size: int = dataclasses.field(default_factory=lambda: _env_int("B200AR_LAMPORT_MAX_SIZE", 1 << 20))
+    lamport_max_size: int = dataclasses.field(default_factory=lambda: _env_int("B200AR_LAMPORT_MAX_SIZE", 4 << 20))
     # Barrier wait limit before a kernel reports a timeout.
     timeout_ms: int = dataclasses.field(default_factory=lambda: _env_int("B200AR_TIMEOUT_MS", 10000))
     # Force a variant for every call ("auto", "oneshot_push", "oneshot_pull", "twoshot", "nvls", "nccl").
