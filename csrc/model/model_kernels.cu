@@ -93,114 +93,142 @@ __global__ void rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, const int*
 }
 
 // ------------------------------------------------------------------ decode attention
-// Grid (B, Hkv, splits); 4 warps. Head dim 128: lane holds dims [4 lane, 4 lane + 4).
-// Every warp walks tokens t = split_begin + warp, +4, ...; for each token it
-// scores all G query heads of the group, keeps an online softmax per head.
-constexpr int kAttnWarps = 4;
+// Grid (B, Hkv, splits); one warp per query head of the group (G warps).
+// The CTA walks its token range in chunks of kChunk tokens: K and V of the
+// next chunk are copied to shared memory with cp.async while the current
+// chunk is processed, so global latency is paid once per chunk, not per token.
+//   scores: lane j of warp h scores tokens j and j + 32 of the chunk
+//           (128-wide dot product from shared memory, no shuffles);
+//   softmax: one max and one sum reduction per warp and chunk (online);
+//   P.V:    lane j accumulates head dims [4 j, 4 j + 4) over the chunk.
 constexpr int kHeadDim = 128;
+constexpr int kChunk = 64;
+constexpr int kRowPad = kHeadDim + 8;  // bf16 per shared K/V row (16-byte pad: no bank conflicts)
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  const int n = pred ? 16 : 0;  // zero-fill beyond the sequence
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(gmem), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 template <int G>
-__global__ void __launch_bounds__(kAttnWarps * 32)
+__global__ void __launch_bounds__(G * 32)
     attn_partial_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_cache,
                         const __nv_bfloat16* __restrict__ v_cache, const int* __restrict__ seq_len,
                         float* __restrict__ part_acc, float* __restrict__ part_ml, int hkv, int max_len,
                         int splits, float scale) {
+  extern __shared__ __align__(16) uint8_t attn_smem[];
+  __nv_bfloat16* sK = reinterpret_cast<__nv_bfloat16*>(attn_smem);          // [2][kChunk][kRowPad]
+  __nv_bfloat16* sV = sK + 2 * kChunk * kRowPad;                             // [2][kChunk][kRowPad]
+  float* sQ = reinterpret_cast<float*>(sV + 2 * kChunk * kRowPad);           // [G][kHeadDim]
+  float* sP = sQ + G * kHeadDim;                                             // [G][kChunk]
+
   const int b = blockIdx.x, kh = blockIdx.y, sp = blockIdx.z;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int len = seq_len[b];
   const int t0 = static_cast<int>((static_cast<int64_t>(len) * sp) / splits);
   const int t1 = static_cast<int>((static_cast<int64_t>(len) * (sp + 1)) / splits);
   const int hq = hkv * G;
+  const int64_t tok_stride = static_cast<int64_t>(hkv) * kHeadDim;
+  const __nv_bfloat16* kbase = k_cache + (static_cast<int64_t>(b) * max_len * hkv + kh) * kHeadDim;
+  const __nv_bfloat16* vbase = v_cache + (static_cast<int64_t>(b) * max_len * hkv + kh) * kHeadDim;
 
-  float qv[G][4];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const __nv_bfloat16* qp = q + (static_cast<int64_t>(b) * hq + kh * G + g) * kHeadDim + lane * 4;
-    const uint2 raw = *reinterpret_cast<const uint2*>(qp);
-    qv[g][0] = __uint_as_float(raw.x << 16) * scale;
-    qv[g][1] = __uint_as_float(raw.x & 0xffff0000u) * scale;
-    qv[g][2] = __uint_as_float(raw.y << 16) * scale;
-    qv[g][3] = __uint_as_float(raw.y & 0xffff0000u) * scale;
-  }
-  float m[G], l[G], acc[G][4];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
-    acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
-  }
-  // Each warp takes kUnroll consecutive tokens per step: their K/V loads are
-  // issued together, then scored one after the other (hides load latency).
-  constexpr int kUnroll = 4;
-  for (int tb = t0 + warp * kUnroll; tb < t1; tb += kAttnWarps * kUnroll) {
-    uint2 kr[kUnroll], vr[kUnroll];
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int t = tb + u < t1 ? tb + u : t1 - 1;
-      const int64_t off = ((static_cast<int64_t>(b) * max_len + t) * hkv + kh) * kHeadDim + lane * 4;
-      kr[u] = __ldg(reinterpret_cast<const uint2*>(k_cache + off));
-      vr[u] = __ldg(reinterpret_cast<const uint2*>(v_cache + off));
+  // Queries (scaled) to shared memory as fp32.
+  for (int i = threadIdx.x; i < G * kHeadDim; i += blockDim.x)
+    sQ[i] = __bfloat162float(q[(static_cast<int64_t>(b) * hq + kh * G) * kHeadDim + i]) * scale;
+
+  auto load_chunk = [&](int c, int buf) {
+    const int tb = t0 + c * kChunk;
+    // 64 tokens x 16 packets each for K and for V.
+    for (int i = threadIdx.x; i < kChunk * 16; i += blockDim.x) {
+      const int tt = i >> 4, pk = i & 15;
+      const bool ok = tb + tt < t1;
+      const int64_t off = static_cast<int64_t>(ok ? tb + tt : t0) * tok_stride + pk * 8;
+      cp_async16(sK + (buf * kChunk + tt) * kRowPad + pk * 8, kbase + off, ok);
+      cp_async16(sV + (buf * kChunk + tt) * kRowPad + pk * 8, vbase + off, ok);
     }
+    cp_async_commit();
+  };
+
+  const int nchunks = (t1 - t0 + kChunk - 1) / kChunk;
+  float m = -INFINITY, l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (nchunks > 0) load_chunk(0, 0);
+  for (int c = 0; c < nchunks; ++c) {
+    const int buf = c & 1;
+    if (c + 1 < nchunks) {
+      load_chunk(c + 1, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int tb = t0 + c * kChunk;
+    const __nv_bfloat16* K = sK + buf * kChunk * kRowPad;
+    const __nv_bfloat16* V = sV + buf * kChunk * kRowPad;
+    const float* qh = sQ + h * kHeadDim;
+    // Scores of tokens lane and lane + 32.
+    float sc[2];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      if (tb + u >= t1) break;
-      const float kx[4] = {__uint_as_float(kr[u].x << 16), __uint_as_float(kr[u].x & 0xffff0000u),
-                           __uint_as_float(kr[u].y << 16), __uint_as_float(kr[u].y & 0xffff0000u)};
-      const float vx[4] = {__uint_as_float(vr[u].x << 16), __uint_as_float(vr[u].x & 0xffff0000u),
-                           __uint_as_float(vr[u].y << 16), __uint_as_float(vr[u].y & 0xffff0000u)};
-      float sc[G];
+    for (int u = 0; u < 2; ++u) {
+      const int tt = lane + 32 * u;
+      const uint4* kr = reinterpret_cast<const uint4*>(K + tt * kRowPad);
+      float s = 0.f;
 #pragma unroll
-      for (int g = 0; g < G; ++g) sc[g] = qv[g][0] * kx[0] + qv[g][1] * kx[1] + qv[g][2] * kx[2] + qv[g][3] * kx[3];
-      // All G reductions interleaved (independent shuffle chains).
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int g = 0; g < G; ++g) sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], o);
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float mn = fmaxf(m[g], sc[g]);
-        const float corr = __expf(m[g] - mn);
-        const float pexp = __expf(sc[g] - mn);
-        l[g] = l[g] * corr + pexp;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[g][e] = acc[g][e] * corr + pexp * vx[e];
-        m[g] = mn;
+      for (int d8 = 0; d8 < kHeadDim / 8; ++d8) {
+        float kx[8];
+        unpack_set<__nv_bfloat16>(kr[d8], kx);
+        const float4 qa = *reinterpret_cast<const float4*>(qh + d8 * 8);
+        const float4 qb = *reinterpret_cast<const float4*>(qh + d8 * 8 + 4);
+        s += qa.x * kx[0] + qa.y * kx[1] + qa.z * kx[2] + qa.w * kx[3] + qb.x * kx[4] + qb.y * kx[5] +
+             qb.z * kx[6] + qb.w * kx[7];
       }
+      sc[u] = tb + tt < t1 ? s : -INFINITY;
     }
+    float cmax = fmaxf(sc[0], sc[1]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, o));
+    const float mn = fmaxf(m, cmax);
+    const float corr = m == -INFINITY ? 0.f : __expf(m - mn);
+    const float p0 = sc[0] == -INFINITY ? 0.f : __expf(sc[0] - mn);
+    const float p1 = sc[1] == -INFINITY ? 0.f : __expf(sc[1] - mn);
+    float psum = p0 + p1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+    l = l * corr + psum;
+    m = mn;
+    sP[h * kChunk + lane] = p0;
+    sP[h * kChunk + lane + 32] = p1;
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[e] *= corr;
+    const int lim = min(kChunk, t1 - tb);
+    for (int tt = 0; tt < lim; ++tt) {
+      const float p = sP[h * kChunk + tt];
+      const uint2 vr = *reinterpret_cast<const uint2*>(V + tt * kRowPad + lane * 4);
+      acc[0] += p * __uint_as_float(vr.x << 16);
+      acc[1] += p * __uint_as_float(vr.x & 0xffff0000u);
+      acc[2] += p * __uint_as_float(vr.y << 16);
+      acc[3] += p * __uint_as_float(vr.y & 0xffff0000u);
+    }
+    __syncthreads();  // the buffer is refilled by the next iteration's prefetch
   }
-  // Merge the 4 warps through shared memory.
-  __shared__ float s_m[kAttnWarps][G], s_l[kAttnWarps][G];
-  __shared__ float s_acc[kAttnWarps][G][kHeadDim];
+  const int64_t base = ((static_cast<int64_t>(b) * hq + kh * G + h) * splits + sp);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) part_acc[base * kHeadDim + lane * 4 + e] = acc[e];
   if (lane == 0) {
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      s_m[warp][g] = m[g];
-      s_l[warp][g] = l[g];
-    }
+    part_ml[base * 2 + 0] = m;
+    part_ml[base * 2 + 1] = l;
   }
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) s_acc[warp][g][lane * 4 + e] = acc[g][e];
-  __syncthreads();
-  // Thread layout for the merge: (g, dim) pairs over the 128 threads.
-  for (int idx = threadIdx.x; idx < G * kHeadDim; idx += blockDim.x) {
-    const int g = idx / kHeadDim, dmn = idx % kHeadDim;
-    float mm = -INFINITY;
-    for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, s_m[w][g]);
-    float ll = 0.f, aa = 0.f;
-    for (int w = 0; w < kAttnWarps; ++w) {
-      const float f = s_m[w][g] == -INFINITY ? 0.f : __expf(s_m[w][g] - mm);
-      ll += s_l[w][g] * f;
-      aa += s_acc[w][g][dmn] * f;
-    }
-    const int64_t base = ((static_cast<int64_t>(b) * hq + kh * G + g) * splits + sp);
-    part_acc[base * kHeadDim + dmn] = aa;
-    if (dmn == 0) {
-      part_ml[base * 2 + 0] = mm;
-      part_ml[base * 2 + 1] = ll;
-    }
-  }
+}
+
+template <int G>
+constexpr size_t attn_smem_bytes() {
+  return (4 * kChunk * kRowPad) * sizeof(__nv_bfloat16) + (G * kHeadDim + G * kChunk) * sizeof(float);
 }
 
 // Grid (B * Hq); 128 threads = head dims.
@@ -264,8 +292,9 @@ void rope_kv(const void* qkv, const int* pos, const float* cos_t, const float* s
 
 int attention_splits(int64_t batch, int hkv, int max_len) {
   const int64_t ctas = batch * hkv;
-  int s = static_cast<int>(std::max<int64_t>(1, 2 * 148 / std::max<int64_t>(ctas, 1)));
-  s = std::min(s, std::max(1, max_len / 128));  // at least ~128 tokens per split
+  // About four CTAs per SM, and at least two chunks of tokens per split.
+  int s = static_cast<int>(std::max<int64_t>(1, (4 * 148 + ctas - 1) / std::max<int64_t>(ctas, 1)));
+  s = std::min(s, std::max(1, max_len / (2 * kChunk)));
   return std::min(s, 64);
 }
 
@@ -280,10 +309,24 @@ void decode_attention(const void* q, const void* k_cache, const void* v_cache, c
   const auto* kp = static_cast<const __nv_bfloat16*>(k_cache);
   const auto* vp = static_cast<const __nv_bfloat16*>(v_cache);
   switch (G) {
-    case 1: attn_partial_kernel<1><<<grid, kAttnWarps * 32, 0, s>>>(qp, kp, vp, seq_len, part_acc, part_ml, hkv, max_len, splits, scale); break;
-    case 2: attn_partial_kernel<2><<<grid, kAttnWarps * 32, 0, s>>>(qp, kp, vp, seq_len, part_acc, part_ml, hkv, max_len, splits, scale); break;
-    case 4: attn_partial_kernel<4><<<grid, kAttnWarps * 32, 0, s>>>(qp, kp, vp, seq_len, part_acc, part_ml, hkv, max_len, splits, scale); break;
-    case 8: attn_partial_kernel<8><<<grid, kAttnWarps * 32, 0, s>>>(qp, kp, vp, seq_len, part_acc, part_ml, hkv, max_len, splits, scale); break;
+#define B200AR_ATTN(g)                                                                                      \
+  case g: {                                                                                                 \
+    auto kern = attn_partial_kernel<g>;                                                                     \
+    static bool attr = false;                                                                               \
+    if (!attr) {                                                                                            \
+      B200AR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,                  \
+                                       static_cast<int>(attn_smem_bytes<g>())));                            \
+      attr = true;                                                                                          \
+    }                                                                                                       \
+    kern<<<grid, g * 32, attn_smem_bytes<g>(), s>>>(qp, kp, vp, seq_len, part_acc, part_ml, hkv, max_len,   \
+                                                    splits, scale);                                         \
+    break;                                                                                                  \
+  }
+    B200AR_ATTN(1)
+    B200AR_ATTN(2)
+    B200AR_ATTN(4)
+    B200AR_ATTN(8)
+#undef B200AR_ATTN
     default: throw std::invalid_argument("GQA group size must be 1, 2, 4 or 8");
   }
   B200AR_CUDA(cudaGetLastError());
