@@ -158,15 +158,25 @@ __global__ void __launch_bounds__(kArThreads) twoshot_kernel(ArArgs a) {
   }
 
   // Phase 1: scatter. Rank r's copy of part p goes to row r of p's inbox.
+  // With few ranks, U offsets per thread keep about 8 packets in flight.
+  constexpr int U = N >= 8 ? 1 : (8 + N - 1) / N;
   const int64_t row = static_cast<int64_t>(r) * part;
-  for (int o = threadIdx.x; o < smax; o += blockDim.x) {
-    uint4 v[N];
+  for (int o0 = threadIdx.x; o0 < smax; o0 += U * blockDim.x) {
+    uint4 v[U][N];
 #pragma unroll
-    for (int k = 0; k < N; ++k)
-      if (o < ln[k]) v[k] = ld_in(a.in + (ab[k] + o) * 16);
+    for (int u = 0; u < U; ++u) {
+      const int o = o0 + u * blockDim.x;
 #pragma unroll
-    for (int k = 0; k < N; ++k)
-      if (o < ln[k]) st_cg(peer[k] + (row + rb[k] + o) * 16, v[k]);
+      for (int k = 0; k < N; ++k)
+        if (o < ln[k]) v[u][k] = ld_in(a.in + (ab[k] + o) * 16);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int o = o0 + u * blockDim.x;
+#pragma unroll
+      for (int k = 0; k < N; ++k)
+        if (o < ln[k]) st_cg(peer[k] + (row + rb[k] + o) * 16, v[u][k]);
+    }
   }
 
   bool ok = cta_barrier<N>(a.ctx, j, epoch_of(gen, 0));
@@ -194,14 +204,22 @@ __global__ void __launch_bounds__(kArThreads) twoshot_kernel(ArArgs a) {
   // Phase 3: gather reduced parts of the peers.
   if (ok) {
     const int64_t outbox = static_cast<int64_t>(N) * part;
-    for (int o = threadIdx.x; o < smax; o += blockDim.x) {
-      uint4 v[N];
+    for (int o0 = threadIdx.x; o0 < smax; o0 += U * blockDim.x) {
+      uint4 v[U][N];
 #pragma unroll
-      for (int k = 1; k < N; ++k)
-        if (o < ln[k]) v[k] = ld_cg(peer[k] + (outbox + rb[k] + o) * 16);
+      for (int u = 0; u < U; ++u) {
+        const int o = o0 + u * blockDim.x;
 #pragma unroll
-      for (int k = 1; k < N; ++k)
-        if (o < ln[k]) st_out(a.out + (ab[k] + o) * 16, v[k]);
+        for (int k = 1; k < N; ++k)
+          if (o < ln[k]) v[u][k] = ld_cg(peer[k] + (outbox + rb[k] + o) * 16);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int o = o0 + u * blockDim.x;
+#pragma unroll
+        for (int k = 1; k < N; ++k)
+          if (o < ln[k]) st_out(a.out + (ab[k] + o) * 16, v[u][k]);
+      }
     }
   }
   finish_generation(a.ctx, gen);
