@@ -170,6 +170,9 @@ class CustomAllreduce:
             out = torch.empty_like(inp)
         v = sel.variant_id(variant if variant != "auto" else self.cfg.variant)
         if self._comm is None:
+            # The CPU emulation implements the barrier-based slot variants.
+            if v not in (sel.VARIANTS["oneshot_push"], sel.VARIANTS["oneshot_pull"], sel.VARIANTS["twoshot"]):
+                v = sel.VARIANTS["auto"]
             self._shm.all_reduce(inp, out, v, ctas)
             return out
         if not self.supports(inp) or not self.supports(out) or v == sel.VARIANTS["nccl"]:
