@@ -110,7 +110,9 @@ class OursArm:
         return self.comm.launches
 
     def variant(self, nbytes):
-        return self.comm.plan(nbytes)[0]
+        v = self.comm.plan(nbytes)[0]
+        # Out-of-place calls above the NCCL crossover run the two-shot kernel.
+        return "twoshot" if v == "nccl" else v
 
     def close(self):
         self.comm.close()
