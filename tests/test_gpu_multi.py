@@ -334,3 +334,27 @@ def _ag_gemm(rank, world):
 
 def test_allgather_gemm_fused():
     run_ranks(_ag_gemm, WORLD, backend="nccl")
+
+
+def _nccl_crossover_paths(rank, world):
+    # Above the NCCL crossover: in-place calls go to NCCL, out-of-place calls
+    # run the two-shot kernel (no extra copy); both must give the sum.
+    comm = _comm(rank, max_size=8 << 20)
+    comm.set_selector([(1 << 62, "nccl", 0)])
+    x = (torch.rand(1 << 20, device="cuda") * 2 - 1).to(torch.bfloat16)
+    ref = _oracle(x, world)
+    n0 = comm.launches
+    out = comm.all_reduce(x)
+    torch.cuda.synchronize()
+    assert comm.launches == n0 + 1  # our kernel, not NCCL
+    torch.testing.assert_close(out.float(), ref, atol=2e-2 * world, rtol=1e-2)
+    y = x.clone()
+    comm.all_reduce(y, out=y)
+    torch.cuda.synchronize()
+    assert comm.launches == n0 + 1  # NCCL in place
+    torch.testing.assert_close(y.float(), ref, atol=2e-2 * world, rtol=1e-2)
+    comm.close()
+
+
+def test_nccl_crossover_paths():
+    run_ranks(_nccl_crossover_paths, WORLD, backend="nccl")
