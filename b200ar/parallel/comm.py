@@ -80,7 +80,9 @@ class CustomAllreduce:
         token = [uuid.uuid4().hex[:12] if self.rank == 0 else None]
         dist.broadcast_object_list(token, src=dist.get_global_rank(self.group, 0) if self.group else 0,
                                    group=self.group)
-        self._shm = _C.ShmComm(f"/b200ar-{token[0]}", self.rank, self.world, self.slot_capacity)
+        self.lamport_capacity = (min(self.cfg.lamport_max_size, self.cfg.max_size) + 15) // 16 * 16
+        self._shm = _C.ShmComm(f"/b200ar-{token[0]}", self.rank, self.world, self.slot_capacity,
+                               self.lamport_capacity if self.world > 1 else 0)
         names: List[Optional[str]] = [None] * self.world
         dist.all_gather_object(names, self._shm.segment_name, group=self.group)
         self._shm.connect(names)
@@ -170,8 +172,11 @@ class CustomAllreduce:
             out = torch.empty_like(inp)
         v = sel.variant_id(variant if variant != "auto" else self.cfg.variant)
         if self._comm is None:
-            # The CPU emulation implements the barrier-based slot variants.
-            if v not in (sel.VARIANTS["oneshot_push"], sel.VARIANTS["oneshot_pull"], sel.VARIANTS["twoshot"]):
+            # The CPU emulation implements the slot variants and the Lamport one-shot.
+            cpu_ok = (sel.VARIANTS["oneshot_push"], sel.VARIANTS["oneshot_pull"], sel.VARIANTS["twoshot"],
+                      sel.VARIANTS["lamport"])
+            if v not in cpu_ok or (v == sel.VARIANTS["lamport"]
+                                   and inp.numel() * inp.element_size() > self.lamport_capacity):
                 v = sel.VARIANTS["auto"]
             self._shm.all_reduce(inp, out, v, ctas)
             return out

@@ -292,8 +292,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
 
   // ---- CPU shared-memory backend ----
   py::class_<ShmComm>(m, "ShmComm")
-      .def(py::init<const std::string&, int, int, int64_t>(), py::arg("prefix"), py::arg("rank"), py::arg("world"),
-           py::arg("slot_capacity"))
+      .def(py::init<const std::string&, int, int, int64_t, int64_t>(), py::arg("prefix"), py::arg("rank"),
+           py::arg("world"), py::arg("slot_capacity"), py::arg("lamport_capacity") = 0)
+      .def_property_readonly("lamport_capacity", &ShmComm::lamport_capacity)
       .def_property_readonly("segment_name", &ShmComm::segment_name)
       .def_property_readonly("slot_capacity", &ShmComm::slot_capacity)
       .def_property_readonly("generation", &ShmComm::generation)

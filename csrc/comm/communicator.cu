@@ -392,6 +392,8 @@ void Communicator::check_status() const {
 void Communicator::reset(cudaStream_t stream) {
   B200AR_CUDA(cudaStreamSynchronize(stream));
   B200AR_CUDA(cudaMemset(signals_[rank_], 0, sizeof(Signal)));
+  // Restore the Lamport markers (an aborted call may have left peer packets).
+  if (lam_cap_ > 0) launch_lamport_init(lam_[rank_], lamport_bytes(lam_cap_, world_), nullptr);
   B200AR_CUDA(cudaDeviceSynchronize());
   std::memset(status_host_, 0, sizeof(Status));
 }

@@ -55,12 +55,13 @@ inline void packet_store(char* p, const float* acc) {
 
 }  // namespace
 
-ShmComm::ShmComm(const std::string& prefix, int rank, int world, int64_t slot_capacity)
-    : rank_(rank), world_(world), cap_(slot_capacity), names_(world), base_(world, nullptr) {
+ShmComm::ShmComm(const std::string& prefix, int rank, int world, int64_t slot_capacity, int64_t lamport_capacity)
+    : rank_(rank), world_(world), cap_(slot_capacity), lam_cap_(lamport_capacity), names_(world), base_(world, nullptr) {
   B200AR_CHECK(world >= 1 && world <= kMaxRanks, "world size must be in [1, " << kMaxRanks << "]");
   B200AR_CHECK(rank >= 0 && rank < world, "invalid rank " << rank);
   B200AR_CHECK(slot_capacity > 0 && slot_capacity % 16 == 0, "slot capacity must be a positive multiple of 16");
-  seg_bytes_ = workspace_bytes(cap_);
+  B200AR_CHECK(lamport_capacity >= 0 && lamport_capacity % 16 == 0, "Lamport capacity must be a multiple of 16");
+  seg_bytes_ = workspace_bytes(cap_) + lamport_bytes(lam_cap_, world);
   names_[rank] = prefix + "-r" + std::to_string(rank);
   const int fd = shm_open(names_[rank].c_str(), O_CREAT | O_EXCL | O_RDWR, 0600);
   if (fd < 0) throw std::runtime_error("shm_open(" + names_[rank] + ") failed: " + std::strerror(errno));
@@ -76,6 +77,8 @@ ShmComm::ShmComm(const std::string& prefix, int rank, int world, int64_t slot_ca
     throw std::runtime_error("mmap of shared segment failed");
   }
   std::memset(p, 0, sizeof(Signal));
+  uint32_t* lam = reinterpret_cast<uint32_t*>(static_cast<char*>(p) + workspace_bytes(cap_));
+  for (int64_t i = 0; i < lamport_bytes(lam_cap_, world) / 4; ++i) lam[i] = kLamportMarker;
   base_[rank] = static_cast<char*>(p);
 }
 
@@ -104,6 +107,10 @@ uint32_t ShmComm::generation() const { return ld_acquire(&reinterpret_cast<Signa
 
 void ShmComm::reset() {
   std::memset(base_[rank_], 0, sizeof(Signal));
+  // Peers' packets of an aborted call may sit in the Lamport buffers: restore
+  // the markers so the next Lamport call does not read stale data.
+  uint32_t* lam = reinterpret_cast<uint32_t*>(base_[rank_] + workspace_bytes(cap_));
+  for (int64_t i = 0; i < lamport_bytes(lam_cap_, world_) / 4; ++i) lam[i] = kLamportMarker;
   std::atomic_thread_fence(std::memory_order_seq_cst);
   status_ = Status{};
   skip_ = 0;
@@ -209,7 +216,7 @@ void ShmComm::run(const char* in, char* out, int64_t P, int variant, int G) {
         std::memcpy(out + (pb + sb) * 16, slotp(p) + (static_cast<int64_t>(N) * part + sb) * 16, sl * 16);
       }
     } else {
-      throw std::invalid_argument("CPU backend supports variants push (1), pull (2) and two-shot (3)");
+      throw std::invalid_argument("CPU backend supports variants push (1), pull (2), two-shot (3), Lamport (8)");
     }
   }
   if (skip) --skip_;
@@ -218,6 +225,93 @@ void ShmComm::run(const char* in, char* out, int64_t P, int variant, int G) {
     std::ostringstream os;
     os << "b200ar(cpu): rank " << status_.rank << " timed out waiting for rank " << status_.peer << " (cta "
        << status_.cta << ", epoch " << status_.epoch << ", last seen " << status_.seen << ")";
+    throw CommTimeout(os.str());
+  }
+}
+
+// Lamport one-shot, as oneshot_lamport_kernel: write own packets (-0.0 turned
+// into +0.0) into every rank's buffer gen % 3, poll own buffer until no word
+// is the marker, sum in rank order, restore the markers. Emulated CTAs run
+// one after the other; CTA j only waits for the peers' CTA j packets.
+template <typename T>
+void ShmComm::run_lamport(const char* in, char* out, int64_t P, int G) {
+  Signal* self = reinterpret_cast<Signal*>(base_[rank_]);
+  const uint32_t gen = self->gen;
+  const int N = world_;
+  const int r = rank_;
+  const int64_t buf = workspace_bytes(cap_) + static_cast<int64_t>(gen % kLamportBuffers) * N * lam_cap_;
+  constexpr int E = elems<T>();
+  float acc[E];
+  const bool skip = skip_ > 0;
+  bool ok = true;
+  for (int j = 0; j < G && ok; ++j) {
+    const int64_t b = part_begin(P, G, j), e = part_begin(P, G, j + 1);
+    for (int64_t i = b; i < e; ++i) {
+      uint32_t w[4];
+      std::memcpy(w, in + i * 16, 16);
+      for (int k = 0; k < 4; ++k) {
+        if (sizeof(T) == 4) {
+          if (w[k] == kLamportMarker) w[k] = 0;
+        } else {
+          if ((w[k] & 0xffffu) == 0x8000u) w[k] &= 0xffff0000u;
+          if ((w[k] >> 16) == 0x8000u) w[k] &= 0x0000ffffu;
+        }
+      }
+      for (int p = 0; p < N; ++p) {
+        uint32_t* dst = reinterpret_cast<uint32_t*>(base_[p] + buf + static_cast<int64_t>(r) * lam_cap_ + i * 16);
+        for (int k = 0; k < 4; ++k) __atomic_store_n(dst + k, w[k], __ATOMIC_RELAXED);
+      }
+    }
+    if (skip) continue;
+    for (int64_t i = b; i < e && ok; ++i) {
+      for (int q = 0; q < N && ok; ++q) {
+        uint32_t* src = reinterpret_cast<uint32_t*>(base_[r] + buf + static_cast<int64_t>(q) * lam_cap_ + i * 16);
+        const auto start = std::chrono::steady_clock::now();
+        uint32_t spins = 0;
+        for (;;) {
+          bool ready = true;
+          for (int k = 0; k < 4; ++k) ready &= __atomic_load_n(src + k, __ATOMIC_ACQUIRE) != kLamportMarker;
+          if (ready) break;
+          if ((++spins & 255u) == 0u) {
+            std::this_thread::yield();
+            const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                                std::chrono::steady_clock::now() - start).count();
+            if (ms > timeout_ms_) {
+              if (status_.code == kStatusOk) {
+                status_.code = kStatusTimeout;
+                status_.rank = r;
+                status_.peer = q;
+                status_.cta = j;
+                status_.epoch = gen;
+              }
+              ++status_.count;
+              ok = false;
+              break;
+            }
+          }
+        }
+      }
+      if (!ok) break;
+      for (int q = 0; q < N; ++q) {
+        const char* src = base_[r] + buf + static_cast<int64_t>(q) * lam_cap_ + i * 16;
+        if (q == 0)
+          packet_set<T>(src, acc);
+        else
+          packet_add<T>(src, acc);
+      }
+      packet_store<T>(out + i * 16, acc);
+      for (int q = 0; q < N; ++q) {
+        uint32_t* src = reinterpret_cast<uint32_t*>(base_[r] + buf + static_cast<int64_t>(q) * lam_cap_ + i * 16);
+        for (int k = 0; k < 4; ++k) __atomic_store_n(src + k, kLamportMarker, __ATOMIC_RELAXED);
+      }
+    }
+  }
+  if (skip) --skip_;
+  __atomic_store_n(&self->gen, gen + 1u, __ATOMIC_RELEASE);
+  if (!ok) {
+    std::ostringstream os;
+    os << "b200ar(cpu): rank " << status_.rank << " timed out waiting for rank " << status_.peer
+       << " (Lamport packets, cta " << status_.cta << ", generation " << status_.epoch << ")";
     throw CommTimeout(os.str());
   }
 }
@@ -234,6 +328,18 @@ void ShmComm::allreduce(const void* in, void* out, int64_t bytes, DType dt, int 
     return;
   }
   if (variant == kAuto) variant = bytes <= 256 * 1024 ? kOneshotPush : kTwoshot;
+  if (variant == kLamport) {
+    B200AR_CHECK(bytes <= lam_cap_, "message of " << bytes << " bytes exceeds the Lamport capacity " << lam_cap_);
+    const int G = ctas > 0 ? std::min(ctas, kMaxCTAs) : 4;
+    const char* i = static_cast<const char*>(in);
+    char* o = static_cast<char*>(out);
+    switch (dt) {
+      case DType::kFloat32: run_lamport<float>(i, o, bytes / 16, G); break;
+      case DType::kFloat16: run_lamport<c10::Half>(i, o, bytes / 16, G); break;
+      case DType::kBFloat16: run_lamport<c10::BFloat16>(i, o, bytes / 16, G); break;
+    }
+    return;
+  }
   const int64_t need = variant_slot_bytes(variant, bytes, world_);
   if (need > cap_) {
     variant = variant_slot_bytes(kTwoshot, bytes, world_) <= cap_ ? kTwoshot : kOneshotPull;

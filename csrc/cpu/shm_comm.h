@@ -23,8 +23,10 @@ namespace b200ar {
 
 class ShmComm {
  public:
-  // Creates (and zeroes) this rank's segment `<prefix>-r<rank>`.
-  ShmComm(const std::string& prefix, int rank, int world, int64_t slot_capacity);
+  // Creates (and zeroes) this rank's segment `<prefix>-r<rank>`. With
+  // lamport_capacity > 0 the segment also holds the Lamport buffers
+  // (layout.h), filled with the marker.
+  ShmComm(const std::string& prefix, int rank, int world, int64_t slot_capacity, int64_t lamport_capacity = 0);
   ~ShmComm();
   ShmComm(const ShmComm&) = delete;
   ShmComm& operator=(const ShmComm&) = delete;
@@ -39,6 +41,7 @@ class ShmComm {
 
   void set_timeout_ms(int64_t ms) { timeout_ms_ = ms; }
   int64_t slot_capacity() const { return cap_; }
+  int64_t lamport_capacity() const { return lam_cap_; }
   const Status& status() const { return status_; }
   uint32_t generation() const;
   // Zeroes this rank's signal block and clears the status (call collectively).
@@ -50,11 +53,14 @@ class ShmComm {
  private:
   bool barrier(int cta, uint32_t epoch);
   template <typename T>
+  void run_lamport(const char* in, char* out, int64_t packets, int ctas);
+  template <typename T>
   void run(const char* in, char* out, int64_t packets, int variant, int ctas);
 
   int rank_;
   int world_;
   int64_t cap_;
+  int64_t lam_cap_ = 0;
   int64_t seg_bytes_;
   std::vector<std::string> names_;
   std::vector<char*> base_;  // mapped segment of every rank

@@ -7,7 +7,7 @@ import torch.distributed as dist
 
 from dist_util import run_ranks
 
-VARIANTS = ["oneshot_push", "oneshot_pull", "twoshot"]
+VARIANTS = ["oneshot_push", "oneshot_pull", "twoshot", "lamport"]
 
 
 def _baseline_config1(rank, world):
@@ -66,7 +66,7 @@ def _many_calls(rank, world):
     comm = CustomAllreduce(device="cpu", max_size=1 << 20)
     for i in range(300):
         numel = 16 if i % 2 == 0 else 7168
-        variant = VARIANTS[i % 3]
+        variant = VARIANTS[i % len(VARIANTS)]
         x = torch.full((numel,), float(rank + 1) + i * 0.25, dtype=torch.float32)
         out = comm.all_reduce(x, variant=variant, ctas=1 + i % 4)
         want = sum(float(r + 1) + i * 0.25 for r in range(world))
@@ -120,6 +120,19 @@ def _timeout_and_reset(rank, world):
     comm.reset()
     out = comm.all_reduce(torch.full((2048,), float(rank)), variant="twoshot")
     assert torch.all(out == sum(range(world)))
+    # A Lamport call whose peer never writes also times out; after reset the
+    # buffers hold markers again and Lamport calls give exact sums.
+    if rank == 1:
+        comm._shm.inject_skip(1)
+    try:
+        comm.all_reduce(x, variant="lamport")
+    except CommTimeoutError:
+        pass
+    dist.barrier()
+    comm.reset()
+    for i in range(6):
+        out = comm.all_reduce(torch.full((4096,), float(rank + i)), variant="lamport")
+        assert torch.all(out == sum(r + i for r in range(world))), i
     comm.close()
 
 
