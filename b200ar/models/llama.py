@@ -1,6 +1,6 @@
 """Tensor-parallel Llama-3-70B-shaped decoder slice built on b200ar kernels.
 
-hidden 8192, 64 query / 8 KV heads of 128, RoPE
+Benchmark configuration: hidden 8192, 64 query / 8 KV heads of 128, RoPE
 theta 500000, SwiGLU FFN 28672, RMSNorm eps 1e-5, 8 layers, random-init bf16
 weights ~ N(0, 0.02), KV cache pre-filled with 2048 random tokens, decode at
 batch 1 / 8 / 32 / 64 under CUDA graphs, two fused all-reduces per layer.

@@ -1,6 +1,6 @@
 """Headline benchmark: bf16 sum all-reduce p50 latency vs message size.
 
-Metric: "bf16 allreduce p50 µs vs size at 2/4/8 GPU vs ref
+Headline metric: "bf16 allreduce p50 µs vs size at 2/4/8 GPU vs ref
 kernel+NCCL; crossover size". Sizes 4 KB .. 256 MB (powers of two), bf16 values
 uniform[-1, 1] seeded 1234 + rank, eager and CUDA-graph modes.
 

@@ -1,4 +1,4 @@
-"""fused all-reduce + residual add + RMSNorm at the
+"""Benchmark configuration: fused all-reduce + residual add + RMSNorm at the
 Llama-3-70B hidden size (8192), T in {1, 8, 32, 128, 512}.
 
 Per rank: partial [T, 8192] ~ N(0,1), residual [T, 8192] ~ N(0,1),

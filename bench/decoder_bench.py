@@ -1,4 +1,4 @@
-"""TP Llama-3-70B-shaped decoder slice, decode step.
+"""Benchmark configuration: TP Llama-3-70B-shaped decoder slice, decode step.
 
 8 layers, hidden 8192, 64/8 heads of 128, FFN 28672, KV cache pre-filled with
 2048 random tokens, random-init weights; batch 1 / 8 / 32 / 64; both the

@@ -1,4 +1,4 @@
-"""TP row-parallel down projection fused with its all-reduce.
+"""Benchmark configuration: TP row-parallel down projection fused with its all-reduce.
 
 Per rank x [M, 3584] ~ N(0,1), W [8192, 3584] ~ N(0, 0.02), M in {16, 128, 1024,
 8192}. Times (p50 of max over ranks, L2 flushed before every call):

@@ -1,5 +1,5 @@
-"""tcgen05 GEMM throughput vs cuBLAS (torch.matmul) on the BASELINE config-4
-shapes (x [M, 3584] @ W[8192, 3584]^T, M in {16, 128, 1024, 8192}) plus a
+"""tcgen05 GEMM throughput vs cuBLAS (torch.matmul) on the row-parallel
+down-projection shapes (x [M, 3584] @ W[8192, 3584]^T, M in {16, 128, 1024, 8192}) plus a
 square 8192^3 case. CUDA-event timing, L2 flushed before every call, p50.
 
     python bench/gemm_bench.py [--iters 50]

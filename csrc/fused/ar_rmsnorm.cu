@@ -5,8 +5,8 @@
 //
 // Outputs: y and the new residual z (may alias the residual input). The
 // reference has no fused op (its kernels only sum, pcie_allreduce.cu:171-276);
-// this is the "all-reduce fused with residual-add + RMSNorm" path of the
-// BASELINE configuration, built on the same signal/slot protocol as the plain
+// this is the all-reduce fused with residual-add + RMSNorm of tensor-parallel
+// decode, built on the same signal/slot protocol as the plain
 // all-reduce (generation counter, per-CTA bounded barriers, double-buffered slots).
 //
 // One CTA owns whole rows: a row of H bf16 values is H/8 16-byte packets and

@@ -8,7 +8,7 @@
 //                  query heads of its group
 //   silu_mul       y = silu(gate) * up for gate_up = [gate | up]
 // All kernels move 16-byte packets and accumulate in fp32. The reference
-// library has no model code; these serve BASELINE configuration 5.
+// library has no model code; these serve the TP decoder slice.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 

@@ -11,7 +11,7 @@ VARIANTS = ["oneshot_push", "oneshot_pull", "twoshot", "lamport"]
 
 
 def _baseline_config1(rank, world):
-    # bf16 [1024, 1024] ~ N(0, 1) seeded 1234 + rank, fp32 oracle, atol 2e-2.
+    # Benchmark configuration: bf16 [1024, 1024] ~ N(0, 1) seeded 1234 + rank, fp32 oracle, atol 2e-2.
     from b200ar import CustomAllreduce
 
     comm = CustomAllreduce(group=None, device="cpu", max_size=4 << 20)

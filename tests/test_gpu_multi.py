@@ -208,7 +208,7 @@ def test_stress_mixed_sizes():
 
 
 def _fused_rmsnorm(rank, world):
-    # BASELINE config 3 shapes: partial [T, 8192] ~ N(0,1), residual ~ N(0,1),
+    # Benchmark shapes: partial [T, 8192] ~ N(0,1), residual ~ N(0,1),
     # gamma = 1 + 0.01 N(0,1), eps 1e-5, T in {1, 8, 32, 128, 512}.
     from b200ar.ops.fused import ref_ar_residual_rmsnorm
 
@@ -274,7 +274,7 @@ def test_nvls_multimem():
 
 
 def _gemm_allreduce(rank, world):
-    # BASELINE config 4 (down projection): x [M, 3584] ~ N(0,1), W [8192, 3584] ~ N(0, 0.02).
+    # (down projection): x [M, 3584] ~ N(0,1), W [8192, 3584] ~ N(0, 0.02).
     from b200ar.ops.gemm import check_errors, error_word
 
     comm = _comm(rank, max_size=160 << 20)
