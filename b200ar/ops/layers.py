@@ -55,7 +55,10 @@ def ref_rope(x, pos, rot: RotaryTable):
     return torch.cat([x0 * c - x1 * s, x1 * c + x0 * s], dim=-1)
 
 
-_ATTN_WS: Dict[Tuple[int, int], Tuple[torch.Tensor, torch.Tensor]] = {}
+# Per (device, partial count, counter count): fp32 partial outputs, fp32
+# (max, sum) pairs and the int32 per-(batch, KV head) arrival counters, which
+# start at zero and are re-armed by the kernel itself.
+_ATTN_WS: Dict[Tuple[int, int, int], Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = {}
 
 
 def decode_attention(q, k_cache, v_cache, seq_len, hq: int, hkv: int, out=None, splits: int = 0):
@@ -65,12 +68,13 @@ def decode_attention(q, k_cache, v_cache, seq_len, hq: int, hkv: int, out=None, 
         out = torch.empty(b, hq * 128, dtype=q.dtype, device=q.device)
     if splits <= 0:
         splits = _C.attention_splits(b, hkv, k_cache.shape[1])
-    key = (q.device.index or 0, b * hq * splits)
+    key = (q.device.index or 0, b * hq * splits, b * hkv)
     if key not in _ATTN_WS:
         _ATTN_WS[key] = (torch.empty(b * hq * splits * 128, dtype=torch.float32, device=q.device),
-                         torch.empty(b * hq * splits * 2, dtype=torch.float32, device=q.device))
-    acc, ml = _ATTN_WS[key]
-    _C.decode_attention(q, k_cache, v_cache, seq_len, out, acc, ml, hq, hkv, splits, 1.0 / math.sqrt(128))
+                         torch.empty(b * hq * splits * 2, dtype=torch.float32, device=q.device),
+                         torch.zeros(b * hkv, dtype=torch.int32, device=q.device))
+    acc, ml, cnt = _ATTN_WS[key]
+    _C.decode_attention(q, k_cache, v_cache, seq_len, out, acc, ml, cnt, hq, hkv, splits, 1.0 / math.sqrt(128))
     return out
 
 

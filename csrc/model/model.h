@@ -12,8 +12,8 @@ void rope_kv(const void* qkv, const int* pos, const float* cos_t, const float* s
              void* v_cache, int64_t batch, int hq, int hkv, int head_dim, int max_len, cudaStream_t s);
 int attention_splits(int64_t batch, int hkv, int max_len);
 void decode_attention(const void* q, const void* k_cache, const void* v_cache, const int* seq_len, void* out,
-                      float* part_acc, float* part_ml, int64_t batch, int hq, int hkv, int head_dim, int max_len,
-                      int splits, float scale, cudaStream_t s);
+                      float* part_acc, float* part_ml, unsigned* done_count, int64_t batch, int hq, int hkv,
+                      int head_dim, int max_len, int splits, float scale, cudaStream_t s);
 void silu_mul(const void* gate_up, void* y, int64_t rows, int64_t inter, cudaStream_t s);
 
 }  // namespace b200ar

@@ -3,9 +3,10 @@
 //   rope_kv        rotary embedding of q and k (rotate-half convention), q to a
 //                  contiguous buffer, k and v written into the KV cache at `pos`
 //   attention      GQA decode attention, split over the KV length
-//                  (flash-decoding): partial softmax state per split, then a
-//                  combine kernel; K/V of one KV head are read once for all the
-//                  query heads of its group
+//                  (flash-decoding): partial softmax state per split; the
+//                  last split CTA of each (batch, KV head) to finish merges the
+//                  partials (L2-resident) in the same launch; K/V of one KV
+//                  head are read once for all the query heads of its group
 //   silu_mul       y = silu(gate) * up for gate_up = [gate | up]
 // All kernels move 16-byte packets and accumulate in fp32. The reference
 // library has no model code; these serve the TP decoder slice.
@@ -120,7 +121,8 @@ template <int G>
 __global__ void __launch_bounds__(G * 32)
     attn_partial_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_cache,
                         const __nv_bfloat16* __restrict__ v_cache, const int* __restrict__ seq_len,
-                        float* __restrict__ part_acc, float* __restrict__ part_ml, int hkv, int max_len,
+                        float* __restrict__ part_acc, float* __restrict__ part_ml,
+                        unsigned* __restrict__ done_count, __nv_bfloat16* __restrict__ out, int hkv, int max_len,
                         int splits, float scale) {
   extern __shared__ __align__(16) uint8_t attn_smem[];
   __nv_bfloat16* sK = reinterpret_cast<__nv_bfloat16*>(attn_smem);          // [2][kChunk][kRowPad]
@@ -217,39 +219,51 @@ __global__ void __launch_bounds__(G * 32)
     }
     __syncthreads();  // the buffer is refilled by the next iteration's prefetch
   }
-  const int64_t base = ((static_cast<int64_t>(b) * hq + kh * G + h) * splits + sp);
-#pragma unroll
-  for (int e = 0; e < 4; ++e) part_acc[base * kHeadDim + lane * 4 + e] = acc[e];
+  const int64_t head = static_cast<int64_t>(b) * hq + kh * G + h;
+  const int64_t base = head * splits + sp;
+  *reinterpret_cast<float4*>(part_acc + base * kHeadDim + lane * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
   if (lane == 0) {
     part_ml[base * 2 + 0] = m;
     part_ml[base * 2 + 1] = l;
   }
+
+  // Merge: the split CTA that finishes last combines all partials of its
+  // (batch, KV head) and re-arms the counter for the next launch (counters
+  // start at zero). Fence, then count: the classic last-block reduction.
+  __shared__ unsigned is_last;
+  __threadfence();
+  __syncthreads();
+  unsigned* cnt = done_count + static_cast<int64_t>(b) * hkv + kh;
+  if (threadIdx.x == 0) is_last = atomicAdd(cnt, 1u) == static_cast<unsigned>(splits - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  if (threadIdx.x == 0) *cnt = 0u;
+  const float* ml = part_ml + head * splits * 2;
+  const float* pa = part_acc + head * splits * kHeadDim + lane * 4;
+  float mm = -INFINITY;
+  for (int s2 = 0; s2 < splits; ++s2) mm = fmaxf(mm, __ldcg(ml + 2 * s2));
+  float ll = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+  for (int s2 = 0; s2 < splits; ++s2) {
+    const float ms = __ldcg(ml + 2 * s2);
+    const float f = ms == -INFINITY ? 0.f : __expf(ms - mm);
+    ll += __ldcg(ml + 2 * s2 + 1) * f;
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(pa + static_cast<int64_t>(s2) * kHeadDim));
+    o[0] += a.x * f;
+    o[1] += a.y * f;
+    o[2] += a.z * f;
+    o[3] += a.w * f;
+  }
+  const float inv = ll > 0.f ? 1.f / ll : 0.f;
+  __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(out + head * kHeadDim + lane * 4);
+  dst[0] = __floats2bfloat162_rn(o[0] * inv, o[1] * inv);
+  dst[1] = __floats2bfloat162_rn(o[2] * inv, o[3] * inv);
 }
 
 template <int G>
 constexpr size_t attn_smem_bytes() {
   return (4 * kChunk * kRowPad) * sizeof(__nv_bfloat16) + (G * kHeadDim + G * kChunk) * sizeof(float);
-}
-
-// Grid (B * Hq); 128 threads = head dims.
-__global__ void attn_combine_kernel(const float* __restrict__ part_acc, const float* __restrict__ part_ml,
-                                    __nv_bfloat16* __restrict__ out, int splits) {
-  const int64_t bh = blockIdx.x;
-  const int dmn = threadIdx.x;
-  const float* ml = part_ml + bh * splits * 2;
-  const float* pa = part_acc + bh * splits * kHeadDim + dmn;
-  float mm = -INFINITY;
-#pragma unroll 8
-  for (int s = 0; s < splits; ++s) mm = fmaxf(mm, ml[2 * s]);
-  float ll = 0.f, aa = 0.f;
-#pragma unroll 8
-  for (int s = 0; s < splits; ++s) {
-    const float ms = ml[2 * s];
-    const float f = ms == -INFINITY ? 0.f : __expf(ms - mm);
-    ll += ml[2 * s + 1] * f;
-    aa += pa[static_cast<int64_t>(s) * kHeadDim] * f;
-  }
-  out[bh * kHeadDim + dmn] = __float2bfloat16_rn(ll > 0.f ? aa / ll : 0.f);
 }
 
 // ------------------------------------------------------------------ SiLU gate
@@ -299,8 +313,8 @@ int attention_splits(int64_t batch, int hkv, int max_len) {
 }
 
 void decode_attention(const void* q, const void* k_cache, const void* v_cache, const int* seq_len, void* out,
-                      float* part_acc, float* part_ml, int64_t batch, int hq, int hkv, int head_dim, int max_len,
-                      int splits, float scale, cudaStream_t s) {
+                      float* part_acc, float* part_ml, unsigned* done_count, int64_t batch, int hq, int hkv,
+                      int head_dim, int max_len, int splits, float scale, cudaStream_t s) {
   B200AR_CHECK(head_dim == kHeadDim, "decode attention is built for head_dim 128");
   B200AR_CHECK(hq % hkv == 0, "query heads must be a multiple of KV heads");
   const int G = hq / hkv;
@@ -318,8 +332,9 @@ void decode_attention(const void* q, const void* k_cache, const void* v_cache, c
                                        static_cast<int>(attn_smem_bytes<g>())));                            \
       attr = true;                                                                                          \
     }                                                                                                       \
-    kern<<<grid, g * 32, attn_smem_bytes<g>(), s>>>(qp, kp, vp, seq_len, part_acc, part_ml, hkv, max_len,   \
-                                                    splits, scale);                                         \
+    kern<<<grid, g * 32, attn_smem_bytes<g>(), s>>>(qp, kp, vp, seq_len, part_acc, part_ml, done_count,     \
+                                                    static_cast<__nv_bfloat16*>(out), hkv, max_len, splits, \
+                                                    scale);                                                 \
     break;                                                                                                  \
   }
     B200AR_ATTN(1)
@@ -329,9 +344,6 @@ void decode_attention(const void* q, const void* k_cache, const void* v_cache, c
 #undef B200AR_ATTN
     default: throw std::invalid_argument("GQA group size must be 1, 2, 4 or 8");
   }
-  B200AR_CUDA(cudaGetLastError());
-  attn_combine_kernel<<<static_cast<unsigned>(batch * hq), kHeadDim, 0, s>>>(part_acc, part_ml,
-                                                                             static_cast<__nv_bfloat16*>(out), splits);
   B200AR_CUDA(cudaGetLastError());
 }
 

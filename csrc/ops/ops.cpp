@@ -59,13 +59,17 @@ void register_ops(py::module& m) {
   m.def(
       "decode_attention",
       [stream](const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache, const at::Tensor& seq_len,
-               at::Tensor& out, at::Tensor& part_acc, at::Tensor& part_ml, int hq, int hkv, int splits, double scale) {
+               at::Tensor& out, at::Tensor& part_acc, at::Tensor& part_ml, at::Tensor& done_count, int hq, int hkv,
+               int splits, double scale) {
         const int64_t b = q.size(0);
         TORCH_CHECK(part_acc.numel() >= b * hq * splits * 128 && part_ml.numel() >= b * hq * splits * 2,
                     "attention workspace too small");
+        TORCH_CHECK(done_count.scalar_type() == at::kInt && done_count.numel() >= b * hkv,
+                    "attention counters must be int32 with one entry per (batch, KV head), zero at first use");
         const at::cuda::OptionalCUDAGuard guard(device_of(q));
         b200ar::decode_attention(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), seq_len.data_ptr<int>(),
-                                 out.data_ptr(), part_acc.data_ptr<float>(), part_ml.data_ptr<float>(), b, hq, hkv,
+                                 out.data_ptr(), part_acc.data_ptr<float>(), part_ml.data_ptr<float>(),
+                                 reinterpret_cast<unsigned*>(done_count.data_ptr<int>()), b, hq, hkv,
                                  128, static_cast<int>(k_cache.size(1)), splits, static_cast<float>(scale), stream());
       });
   m.def(

@@ -56,3 +56,31 @@ def test_silu_mul():
 
     gu = torch.randn(5, 2 * 3584, device="cuda").to(torch.bfloat16)
     torch.testing.assert_close(silu_mul(gu).float(), ref_silu_mul(gu).float(), atol=2e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("splits", [1, 3, 64])
+def test_decode_attention_merge_rearms(splits):
+    """The last split CTA merges the partials and re-arms its counter: repeated
+    eager calls and CUDA-graph replays must keep matching the reference."""
+    from b200ar.ops.layers import decode_attention, ref_decode_attention
+
+    b, hq, hkv, L = 4, 8, 1, 1024 + 40
+    q = torch.randn(b, hq, 128, device="cuda").to(torch.bfloat16)
+    kc = torch.randn(b, L, hkv, 128, device="cuda").to(torch.bfloat16)
+    vc = torch.randn(b, L, hkv, 128, device="cuda").to(torch.bfloat16)
+    seq = torch.tensor([L, L - 7, 1, 0], dtype=torch.int32, device="cuda")
+    out = torch.empty(b, hq * 128, dtype=torch.bfloat16, device="cuda")
+    for _ in range(3):
+        decode_attention(q, kc, vc, seq, hq, hkv, out=out, splits=splits)
+    ref = ref_decode_attention(q, kc, vc, seq, hq, hkv)
+    torch.testing.assert_close(out.float()[:3], ref[:3], atol=2e-2, rtol=2e-2)
+    assert torch.equal(out[3], torch.zeros_like(out[3]))  # empty sequence -> zeros
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        decode_attention(q, kc, vc, seq, hq, hkv, out=out, splits=splits)
+    for _ in range(3):
+        q.copy_(torch.randn_like(q, dtype=torch.float32).to(torch.bfloat16))
+        g.replay()
+        torch.cuda.synchronize()
+        ref = ref_decode_attention(q, kc, vc, seq, hq, hkv)
+        torch.testing.assert_close(out.float()[:3], ref[:3], atol=2e-2, rtol=2e-2)
