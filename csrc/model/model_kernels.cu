@@ -3,7 +3,8 @@
 //   rope_kv        rotary embedding of q and k (rotate-half convention), q to a
 //                  contiguous buffer, k and v written into the KV cache at `pos`
 //   attention      GQA decode attention, split over the KV length
-//                  (flash-decoding): partial softmax state per split; the
+//                  (flash-decoding) with both products on the tensor cores
+//                  (mma.sync m16n8k16): partial softmax state per split; the
 //                  last split CTA of each (batch, KV head) to finish merges the
 //                  partials (L2-resident) in the same launch; K/V of one KV
 //                  head are read once for all the query heads of its group
@@ -94,17 +95,31 @@ __global__ void rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, const int*
 }
 
 // ------------------------------------------------------------------ decode attention
-// Grid (B, Hkv, splits); one warp per query head of the group (G warps).
-// The CTA walks its token range in chunks of kChunk tokens: K and V of the
-// next chunk are copied to shared memory with cp.async while the current
-// chunk is processed, so global latency is paid once per chunk, not per token.
-//   scores: lane j of warp h scores tokens j and j + 32 of the chunk
-//           (128-wide dot product from shared memory, no shuffles);
-//   softmax: one max and one sum reduction per warp and chunk (online);
-//   P.V:    lane j accumulates head dims [4 j, 4 j + 4) over the chunk.
+// Grid (B, Hkv, splits), 4 warps. Both products run on the tensor cores with
+// mma.sync m16n8k16 (bf16 in, fp32 accumulate):
+//   S = Q K^T   rows = the G query heads of the KV head (padded to 16),
+//               columns = tokens; K fragments come from shared memory with
+//               ldmatrix, so every K element is read from shared memory once
+//               per CTA whatever G is;
+//   O += P V    P is the softmax numerator, re-used from the S accumulators as
+//               the A operand (the accumulator layout of m16n8k16 is the A
+//               layout of the next m16n8k16); V fragments via ldmatrix.trans.
+// The CTA walks its token range in chunks of kChunk tokens, double-buffered
+// with cp.async; warp w owns tokens [16 w, 16 w + 16) of every chunk and keeps
+// its own online-softmax state (max and sum in the log2 domain). The four
+// warp states are merged through shared memory at the end, and the last split
+// CTA of the (batch, KV head) merges the split states.
+// Launch bounds: 128 threads; shared memory 68 KB -> 3 CTAs per SM.
 constexpr int kHeadDim = 128;
 constexpr int kChunk = 64;
-constexpr int kRowPad = kHeadDim + 8;  // bf16 per shared K/V row (16-byte pad: no bank conflicts)
+constexpr int kAttnWarps = kChunk / 16;
+constexpr int kAttnThreads = kAttnWarps * 32;
+constexpr int kAttnMaxGroup = 16;
+constexpr int kRowPad = kHeadDim + 8;  // bf16 per shared K/V row: 272 B, so 8 ldmatrix rows hit 8 bank groups
+constexpr size_t kAttnSmem = 4 * kChunk * kRowPad * sizeof(__nv_bfloat16);
+static_assert(kAttnThreads == kHeadDim, "the CTA merge gives one head dimension to each thread");
+static_assert(kAttnWarps * kAttnMaxGroup * (kHeadDim + 2) * sizeof(float) <= kAttnSmem,
+              "the merge area aliases the K/V buffers");
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
   const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
@@ -117,37 +132,56 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <int G>
-__global__ void __launch_bounds__(G * 32)
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* smem) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* smem) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
+}
+// D += A B for one m16n8k16 tile (A row-major 16x16, B column-major 16x8).
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+__global__ void __launch_bounds__(kAttnThreads)
     attn_partial_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_cache,
                         const __nv_bfloat16* __restrict__ v_cache, const int* __restrict__ seq_len,
                         float* __restrict__ part_acc, float* __restrict__ part_ml,
-                        unsigned* __restrict__ done_count, __nv_bfloat16* __restrict__ out, int hkv, int max_len,
-                        int splits, float scale) {
+                        unsigned* __restrict__ done_count, __nv_bfloat16* __restrict__ out, int hkv, int group,
+                        int max_len, int splits, float scale_log2) {
   extern __shared__ __align__(16) uint8_t attn_smem[];
-  __nv_bfloat16* sK = reinterpret_cast<__nv_bfloat16*>(attn_smem);          // [2][kChunk][kRowPad]
-  __nv_bfloat16* sV = sK + 2 * kChunk * kRowPad;                             // [2][kChunk][kRowPad]
-  float* sQ = reinterpret_cast<float*>(sV + 2 * kChunk * kRowPad);           // [G][kHeadDim]
-  float* sP = sQ + G * kHeadDim;                                             // [G][kChunk]
+  __nv_bfloat16* sK = reinterpret_cast<__nv_bfloat16*>(attn_smem);  // [2][kChunk][kRowPad]
+  __nv_bfloat16* sV = sK + 2 * kChunk * kRowPad;                     // [2][kChunk][kRowPad]
 
   const int b = blockIdx.x, kh = blockIdx.y, sp = blockIdx.z;
-  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tig = lane & 3;  // fragment row group and thread-in-group
   const int len = seq_len[b];
   const int t0 = static_cast<int>((static_cast<int64_t>(len) * sp) / splits);
   const int t1 = static_cast<int>((static_cast<int64_t>(len) * (sp + 1)) / splits);
-  const int hq = hkv * G;
+  const int hq = hkv * group;
   const int64_t tok_stride = static_cast<int64_t>(hkv) * kHeadDim;
   const __nv_bfloat16* kbase = k_cache + (static_cast<int64_t>(b) * max_len * hkv + kh) * kHeadDim;
   const __nv_bfloat16* vbase = v_cache + (static_cast<int64_t>(b) * max_len * hkv + kh) * kHeadDim;
 
-  // Queries (scaled) to shared memory as fp32.
-  for (int i = threadIdx.x; i < G * kHeadDim; i += blockDim.x)
-    sQ[i] = __bfloat162float(q[(static_cast<int64_t>(b) * hq + kh * G) * kHeadDim + i]) * scale;
-
   auto load_chunk = [&](int c, int buf) {
     const int tb = t0 + c * kChunk;
-    // 64 tokens x 16 packets each for K and for V.
-    for (int i = threadIdx.x; i < kChunk * 16; i += blockDim.x) {
+    // kChunk tokens x 16 packets each, for K and for V.
+    for (int i = threadIdx.x; i < kChunk * 16; i += kAttnThreads) {
       const int tt = i >> 4, pk = i & 15;
       const bool ok = tb + tt < t1;
       const int64_t off = static_cast<int64_t>(ok ? tb + tt : t0) * tok_stride + pk * 8;
@@ -156,10 +190,29 @@ __global__ void __launch_bounds__(G * 32)
     }
     cp_async_commit();
   };
-
   const int nchunks = (t1 - t0 + kChunk - 1) / kChunk;
-  float m = -INFINITY, l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
   if (nchunks > 0) load_chunk(0, 0);
+
+  // Q as A fragments, one per 16-dim k step: rows g and g + 8 of the group
+  // (zero rows beyond the group size).
+  const __nv_bfloat16* qg = q + (static_cast<int64_t>(b) * hq + static_cast<int64_t>(kh) * group) * kHeadDim;
+  uint32_t qf[kHeadDim / 16][4];
+#pragma unroll
+  for (int ks = 0; ks < kHeadDim / 16; ++ks) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int row = g + 8 * (j & 1);
+      const int col = ks * 16 + 8 * (j >> 1) + 2 * tig;
+      qf[ks][j] = row < group ? __ldg(reinterpret_cast<const unsigned*>(qg + row * kHeadDim + col)) : 0u;
+    }
+  }
+
+  float o[kHeadDim / 8][4];
+#pragma unroll
+  for (int nd = 0; nd < kHeadDim / 8; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};  // rows g and g + 8
+  const int mi = lane >> 3, r8 = lane & 7;                   // ldmatrix: matrix index, row in matrix
+
   for (int c = 0; c < nchunks; ++c) {
     const int buf = c & 1;
     if (c + 1 < nchunks) {
@@ -169,67 +222,107 @@ __global__ void __launch_bounds__(G * 32)
       cp_async_wait<0>();
     }
     __syncthreads();
-    const int tb = t0 + c * kChunk;
-    const __nv_bfloat16* K = sK + buf * kChunk * kRowPad;
-    const __nv_bfloat16* V = sV + buf * kChunk * kRowPad;
-    const float* qh = sQ + h * kHeadDim;
-    // Scores of tokens lane and lane + 32.
-    float sc[2];
+    const int wt = t0 + c * kChunk + warp * 16;  // first token of this warp's slice
+    if (wt < t1) {
+      const __nv_bfloat16* K = sK + (buf * kChunk + warp * 16) * kRowPad;
+      const __nv_bfloat16* V = sV + (buf * kChunk + warp * 16) * kRowPad;
+      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int tt = lane + 32 * u;
-      const uint4* kr = reinterpret_cast<const uint4*>(K + tt * kRowPad);
-      float s = 0.f;
+      for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
-      for (int d8 = 0; d8 < kHeadDim / 8; ++d8) {
-        float kx[8];
-        unpack_set<__nv_bfloat16>(kr[d8], kx);
-        const float4 qa = *reinterpret_cast<const float4*>(qh + d8 * 8);
-        const float4 qb = *reinterpret_cast<const float4*>(qh + d8 * 8 + 4);
-        s += qa.x * kx[0] + qa.y * kx[1] + qa.z * kx[2] + qa.w * kx[3] + qb.x * kx[4] + qb.y * kx[5] +
-             qb.z * kx[6] + qb.w * kx[7];
+        for (int kp = 0; kp < kHeadDim / 32; ++kp) {
+          uint32_t kb[4];  // B fragments of k steps 2 kp and 2 kp + 1 for 8 tokens
+          ldsm_x4(kb, K + (nt * 8 + r8) * kRowPad + kp * 32 + mi * 8);
+          mma_bf16(s[nt], qf[2 * kp], kb[0], kb[1]);
+          mma_bf16(s[nt], qf[2 * kp + 1], kb[2], kb[3]);
+        }
       }
-      sc[u] = tb + tt < t1 ? s : -INFINITY;
-    }
-    float cmax = fmaxf(sc[0], sc[1]);
+      // Scale into the log2 domain and mask tokens past the range.
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, o));
-    const float mn = fmaxf(m, cmax);
-    const float corr = m == -INFINITY ? 0.f : __expf(m - mn);
-    const float p0 = sc[0] == -INFINITY ? 0.f : __expf(sc[0] - mn);
-    const float p1 = sc[1] == -INFINITY ? 0.f : __expf(sc[1] - mn);
-    float psum = p0 + p1;
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
-    l = l * corr + psum;
-    m = mn;
-    sP[h * kChunk + lane] = p0;
-    sP[h * kChunk + lane + 32] = p1;
-    __syncwarp();
+        for (int e = 0; e < 4; ++e)
+          s[nt][e] = wt + nt * 8 + 2 * tig + (e & 1) < t1 ? s[nt][e] * scale_log2 : -INFINITY;
+      uint32_t pa[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) acc[e] *= corr;
-    const int lim = min(kChunk, t1 - tb);
-    for (int tt = 0; tt < lim; ++tt) {
-      const float p = sP[h * kChunk + tt];
-      const uint2 vr = *reinterpret_cast<const uint2*>(V + tt * kRowPad + lane * 4);
-      acc[0] += p * __uint_as_float(vr.x << 16);
-      acc[1] += p * __uint_as_float(vr.x & 0xffff0000u);
-      acc[2] += p * __uint_as_float(vr.y << 16);
-      acc[3] += p * __uint_as_float(vr.y & 0xffff0000u);
+      for (int r = 0; r < 2; ++r) {
+        float mx = fmaxf(fmaxf(s[0][2 * r], s[0][2 * r + 1]), fmaxf(s[1][2 * r], s[1][2 * r + 1]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float mn = fmaxf(m[r], mx);
+        const float corr = m[r] == -INFINITY ? 0.f : exp2f(m[r] - mn);
+        m[r] = mn;
+        float p[2][2];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) p[nt][e] = s[nt][2 * r + e] == -INFINITY ? 0.f : exp2f(s[nt][2 * r + e] - mn);
+        l[r] = l[r] * corr + p[0][0] + p[0][1] + p[1][0] + p[1][1];
+#pragma unroll
+        for (int nd = 0; nd < kHeadDim / 8; ++nd) {
+          o[nd][2 * r] *= corr;
+          o[nd][2 * r + 1] *= corr;
+        }
+        pa[r] = pack_bf16(p[0][0], p[0][1]);      // a0 (row g) / a1 (row g + 8): tokens 2 tig, 2 tig + 1
+        pa[2 + r] = pack_bf16(p[1][0], p[1][1]);  // a2 / a3: tokens 8 + 2 tig, 9 + 2 tig
+      }
+#pragma unroll
+      for (int ndp = 0; ndp < kHeadDim / 16; ++ndp) {
+        uint32_t vb[4];  // B fragments (tokens 0-7, 8-15) of dim tiles 2 ndp and 2 ndp + 1
+        ldsm_x4_trans(vb, V + ((mi & 1) * 8 + r8) * kRowPad + (2 * ndp + (mi >> 1)) * 8);
+        mma_bf16(o[2 * ndp], pa, vb[0], vb[1]);
+        mma_bf16(o[2 * ndp + 1], pa, vb[2], vb[3]);
+      }
     }
     __syncthreads();  // the buffer is refilled by the next iteration's prefetch
   }
-  const int64_t head = static_cast<int64_t>(b) * hq + kh * G + h;
-  const int64_t base = head * splits + sp;
-  *reinterpret_cast<float4*>(part_acc + base * kHeadDim + lane * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-  if (lane == 0) {
-    part_ml[base * 2 + 0] = m;
-    part_ml[base * 2 + 1] = l;
+
+  // Merge the four warp states of this CTA (the merge area aliases K/V).
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    l[r] += __shfl_xor_sync(0xffffffffu, l[r], 1);
+    l[r] += __shfl_xor_sync(0xffffffffu, l[r], 2);
+  }
+  float* sO = reinterpret_cast<float*>(attn_smem);             // [warps][16][kHeadDim]
+  float* sML = sO + kAttnWarps * kAttnMaxGroup * kHeadDim;      // [warps][16][2]
+#pragma unroll
+  for (int nd = 0; nd < kHeadDim / 8; ++nd)
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      sO[(warp * kAttnMaxGroup + g + 8 * (e >> 1)) * kHeadDim + nd * 8 + 2 * tig + (e & 1)] = o[nd][e];
+  if (tig == 0) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      sML[(warp * kAttnMaxGroup + g + 8 * r) * 2 + 0] = m[r];
+      sML[(warp * kAttnMaxGroup + g + 8 * r) * 2 + 1] = l[r];
+    }
+  }
+  __syncthreads();
+  const int64_t head0 = static_cast<int64_t>(b) * hq + static_cast<int64_t>(kh) * group;
+  for (int h = 0; h < group; ++h) {
+    float mm = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, sML[(w * kAttnMaxGroup + h) * 2]);
+    float acc = 0.f, ll = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float mw = sML[(w * kAttnMaxGroup + h) * 2];
+      const float f = mw == -INFINITY ? 0.f : exp2f(mw - mm);
+      acc += sO[(w * kAttnMaxGroup + h) * kHeadDim + threadIdx.x] * f;
+      ll += sML[(w * kAttnMaxGroup + h) * 2 + 1] * f;
+    }
+    const int64_t base = (head0 + h) * splits + sp;
+    part_acc[base * kHeadDim + threadIdx.x] = acc;
+    if (threadIdx.x == 0) {
+      part_ml[base * 2 + 0] = mm;
+      part_ml[base * 2 + 1] = ll;
+    }
   }
 
-  // Merge: the split CTA that finishes last combines all partials of its
-  // (batch, KV head) and re-arms the counter for the next launch (counters
-  // start at zero). Fence, then count: the classic last-block reduction.
+  // Merge the splits: the split CTA that finishes last combines all partials
+  // of its (batch, KV head) and re-arms the counter for the next launch
+  // (counters start at zero). Fence, then count: the classic last-block
+  // reduction.
   __shared__ unsigned is_last;
   __threadfence();
   __syncthreads();
@@ -239,31 +332,29 @@ __global__ void __launch_bounds__(G * 32)
   if (!is_last) return;
   __threadfence();
   if (threadIdx.x == 0) *cnt = 0u;
-  const float* ml = part_ml + head * splits * 2;
-  const float* pa = part_acc + head * splits * kHeadDim + lane * 4;
-  float mm = -INFINITY;
-  for (int s2 = 0; s2 < splits; ++s2) mm = fmaxf(mm, __ldcg(ml + 2 * s2));
-  float ll = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int h = warp; h < group; h += kAttnWarps) {
+    const int64_t head = head0 + h;
+    const float* ml = part_ml + head * splits * 2;
+    const float* pp = part_acc + head * splits * kHeadDim + lane * 4;
+    float mm = -INFINITY;
+    for (int s2 = 0; s2 < splits; ++s2) mm = fmaxf(mm, __ldcg(ml + 2 * s2));
+    float ll = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
-  for (int s2 = 0; s2 < splits; ++s2) {
-    const float ms = __ldcg(ml + 2 * s2);
-    const float f = ms == -INFINITY ? 0.f : __expf(ms - mm);
-    ll += __ldcg(ml + 2 * s2 + 1) * f;
-    const float4 a = __ldcg(reinterpret_cast<const float4*>(pa + static_cast<int64_t>(s2) * kHeadDim));
-    o[0] += a.x * f;
-    o[1] += a.y * f;
-    o[2] += a.z * f;
-    o[3] += a.w * f;
+    for (int s2 = 0; s2 < splits; ++s2) {
+      const float ms = __ldcg(ml + 2 * s2);
+      const float f = ms == -INFINITY ? 0.f : exp2f(ms - mm);
+      ll += __ldcg(ml + 2 * s2 + 1) * f;
+      const float4 a = __ldcg(reinterpret_cast<const float4*>(pp + static_cast<int64_t>(s2) * kHeadDim));
+      acc[0] += a.x * f;
+      acc[1] += a.y * f;
+      acc[2] += a.z * f;
+      acc[3] += a.w * f;
+    }
+    const float inv = ll > 0.f ? 1.f / ll : 0.f;
+    __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(out + head * kHeadDim + lane * 4);
+    dst[0] = __floats2bfloat162_rn(acc[0] * inv, acc[1] * inv);
+    dst[1] = __floats2bfloat162_rn(acc[2] * inv, acc[3] * inv);
   }
-  const float inv = ll > 0.f ? 1.f / ll : 0.f;
-  __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(out + head * kHeadDim + lane * 4);
-  dst[0] = __floats2bfloat162_rn(o[0] * inv, o[1] * inv);
-  dst[1] = __floats2bfloat162_rn(o[2] * inv, o[3] * inv);
-}
-
-template <int G>
-constexpr size_t attn_smem_bytes() {
-  return (4 * kChunk * kRowPad) * sizeof(__nv_bfloat16) + (G * kHeadDim + G * kChunk) * sizeof(float);
 }
 
 // ------------------------------------------------------------------ SiLU gate
@@ -305,9 +396,11 @@ void rope_kv(const void* qkv, const int* pos, const float* cos_t, const float* s
 }
 
 int attention_splits(int64_t batch, int hkv, int max_len) {
-  const int64_t ctas = batch * hkv;
-  // About four CTAs per SM, and at least two chunks of tokens per split.
-  int s = static_cast<int>(std::max<int64_t>(1, (4 * 148 + ctas - 1) / std::max<int64_t>(ctas, 1)));
+  // One wave of 3 CTAs per SM (the kernel's shared memory allows 3), rounded
+  // down so no second partial wave forms; at least two chunks of cache per
+  // split, which keeps the final merge (serial over splits) short.
+  const int64_t ctas = std::max<int64_t>(batch * hkv, 1);
+  int s = static_cast<int>(std::max<int64_t>(1, (3 * 148) / ctas));
   s = std::min(s, std::max(1, max_len / (2 * kChunk)));
   return std::min(s, 64);
 }
@@ -316,34 +409,21 @@ void decode_attention(const void* q, const void* k_cache, const void* v_cache, c
                       float* part_acc, float* part_ml, unsigned* done_count, int64_t batch, int hq, int hkv,
                       int head_dim, int max_len, int splits, float scale, cudaStream_t s) {
   B200AR_CHECK(head_dim == kHeadDim, "decode attention is built for head_dim 128");
-  B200AR_CHECK(hq % hkv == 0, "query heads must be a multiple of KV heads");
-  const int G = hq / hkv;
+  B200AR_CHECK(hkv > 0 && hq % hkv == 0, "query heads must be a multiple of KV heads");
+  const int group = hq / hkv;
+  B200AR_CHECK(group <= kAttnMaxGroup, "GQA group size must be at most 16");
+  B200AR_CHECK(splits >= 1, "splits must be positive");
+  static bool attr = false;
+  if (!attr) {
+    B200AR_CUDA(cudaFuncSetAttribute(attn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(kAttnSmem)));
+    attr = true;
+  }
   const dim3 grid(static_cast<unsigned>(batch), hkv, splits);
-  const auto* qp = static_cast<const __nv_bfloat16*>(q);
-  const auto* kp = static_cast<const __nv_bfloat16*>(k_cache);
-  const auto* vp = static_cast<const __nv_bfloat16*>(v_cache);
-  switch (G) {
-#define B200AR_ATTN(g)                                                                                      \
-  case g: {                                                                                                 \
-    auto kern = attn_partial_kernel<g>;                                                                     \
-    static bool attr = false;                                                                               \
-    if (!attr) {                                                                                            \
-      B200AR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,                  \
-                                       static_cast<int>(attn_smem_bytes<g>())));                            \
-      attr = true;                                                                                          \
-    }                                                                                                       \
-    kern<<<grid, g * 32, attn_smem_bytes<g>(), s>>>(qp, kp, vp, seq_len, part_acc, part_ml, done_count,     \
-                                                    static_cast<__nv_bfloat16*>(out), hkv, max_len, splits, \
-                                                    scale);                                                 \
-    break;                                                                                                  \
-  }
-    B200AR_ATTN(1)
-    B200AR_ATTN(2)
-    B200AR_ATTN(4)
-    B200AR_ATTN(8)
-#undef B200AR_ATTN
-    default: throw std::invalid_argument("GQA group size must be 1, 2, 4 or 8");
-  }
+  attn_partial_kernel<<<grid, kAttnThreads, kAttnSmem, s>>>(
+      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k_cache),
+      static_cast<const __nv_bfloat16*>(v_cache), seq_len, part_acc, part_ml, done_count,
+      static_cast<__nv_bfloat16*>(out), hkv, group, max_len, splits, scale * 1.4426950408889634f);
   B200AR_CUDA(cudaGetLastError());
 }
 
