@@ -3,6 +3,10 @@
 If the shared object is missing, it is built once (under a file lock) unless
 ``B200AR_NO_BUILD=1``. On a machine with a GPU a missing or broken extension is
 an error: b200ar never falls back silently to a pure-PyTorch path.
+
+With ``B200AR_CHECKS=1`` the checked debug build ``b200ar._C_checked`` is
+loaded (and built) instead: its kernels verify access ranges and barrier
+epochs on the device and report violations through the status record.
 """
 
 from __future__ import annotations
@@ -19,7 +23,8 @@ _ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def build_inplace(verbose: bool = False) -> None:
-    """Compiles every native source for sm_100a into ``b200ar/_C*.so``."""
+    """Compiles every native source for sm_100a into ``b200ar/_C*.so`` (the
+    checked build when ``B200AR_CHECKS=1`` is in the environment)."""
     lock_path = os.path.join(_ROOT, ".b200ar_build.lock")
     with open(lock_path, "w") as lock:
         fcntl.flock(lock, fcntl.LOCK_EX)
@@ -32,15 +37,20 @@ def build_inplace(verbose: bool = False) -> None:
             raise RuntimeError(f"building b200ar._C failed:\n{tail}")
 
 
+def module_name() -> str:
+    return "b200ar._C_checked" if os.environ.get("B200AR_CHECKS") == "1" else "b200ar._C"
+
+
 def load():
+    name = module_name()
     try:
-        return importlib.import_module("b200ar._C")
+        return importlib.import_module(name)
     except ImportError:
         if os.environ.get("B200AR_NO_BUILD") == "1":
             raise
     build_inplace()
     importlib.invalidate_caches()
-    return importlib.import_module("b200ar._C")
+    return importlib.import_module(name)
 
 
 _C = load()

@@ -301,6 +301,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("connect", &ShmComm::connect)
       .def("set_timeout_ms", &ShmComm::set_timeout_ms)
       .def("inject_skip", &ShmComm::inject_skip)
+      .def("inject_flag", &ShmComm::inject_flag, py::arg("cta"), py::arg("src"), py::arg("value"))
       .def("reset", &ShmComm::reset)
       .def("status_code", [](ShmComm& c) { return c.status().code; })
       .def("all_reduce",

@@ -39,7 +39,23 @@ struct ArArgs {
   int64_t packets;           // message size in 16-byte packets
   char* lam[kMaxRanks];      // Lamport region of every rank (peer mappings)
   int64_t lam_cap;           // bytes per (buffer, source) block of the Lamport region
+#if defined(B200AR_CHECKS)
+  int64_t slot_cap;          // bytes per slot (checked builds verify footprints against it)
+#endif
 };
+
+// Checked builds: skip the whole call (but keep the generation in step) when
+// the footprint of this call does not fit its buffer. `what` names the buffer
+// in the status record: 1 slot, 2 Lamport block.
+#if defined(B200AR_CHECKS)
+#define B200AR_ENTRY_RANGE(need, cap, what)            \
+  if (!range_ok(a.ctx, (need), (cap), (what))) {       \
+    finish_generation(a.ctx, gen);                     \
+    return;                                            \
+  }
+#else
+#define B200AR_ENTRY_RANGE(need, cap, what)
+#endif
 
 // Fills d[k] = base[(rank + k) % N] without dynamic indexing of a local array.
 template <int N>
@@ -64,6 +80,8 @@ __global__ void __launch_bounds__(kArThreads) oneshot_push_kernel(ArArgs a) {
   const int64_t P = a.packets;
   const int64_t b = part_begin(P, gridDim.x, blockIdx.x);
   const int64_t e = part_begin(P, gridDim.x, blockIdx.x + 1);
+
+  B200AR_ENTRY_RANGE(static_cast<int64_t>(N) * P * 16, a.slot_cap, 1u)
 
   char* dst[N];
   rotate_ptrs<N>(a.slot[slot], r, dst);
@@ -104,6 +122,7 @@ __global__ void __launch_bounds__(kArThreads) oneshot_pull_kernel(ArArgs a) {
   // Peers are summed in rank order 0..N-1 on every rank, so all ranks get
   // bitwise identical results (the reference rotated the order per rank,
   // pcie_allreduce.cu:248-253, which makes results rank dependent).
+  B200AR_ENTRY_RANGE(P * 16, a.slot_cap, 1u)
   char* const* src = a.slot[slot];
   char* mine = src[r];
   for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) st_cg(mine + i * 16, ld_in(a.in + i * 16));
@@ -136,6 +155,7 @@ __global__ void __launch_bounds__(kArThreads) twoshot_kernel(ArArgs a) {
   const int64_t part = (P + N - 1) / N;
   const int G = gridDim.x;
   const int j = blockIdx.x;
+  B200AR_ENTRY_RANGE(static_cast<int64_t>(N + 1) * part * 16, a.slot_cap, 1u)
 
   char* peer[N];  // peer[k] = slot base of rank (r + k) % N
   rotate_ptrs<N>(a.slot[slot], r, peer);
@@ -302,6 +322,7 @@ __global__ void __launch_bounds__(kArThreads) oneshot_lamport_kernel(ArArgs a) {
   const int64_t b = part_begin(P, gridDim.x, blockIdx.x);
   const int64_t e = part_begin(P, gridDim.x, blockIdx.x + 1);
   const int64_t buf_off = static_cast<int64_t>(gen % kLamportBuffers) * N * a.lam_cap;
+  B200AR_ENTRY_RANGE(P * 16, a.lam_cap, 2u)
 
   char* dst[N];
   rotate_ptrs<N>(a.lam, r, dst);

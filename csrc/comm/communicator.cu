@@ -342,6 +342,9 @@ LaunchInfo Communicator::allreduce(cudaStream_t stream, const void* in, void* ou
   a.packets = bytes / 16;
   for (int i = 0; i < world_; ++i) a.lam[i] = lam_[i];
   a.lam_cap = lam_cap_;
+#if defined(B200AR_CHECKS)
+  a.slot_cap = slot_cap_;
+#endif
   if (li.variant == kRegistered) {
     if (capturing) {
       if (arena_next_ + graph_pending_.size() + 1 > arena_end_) throw std::runtime_error("Rank data buffer overflow");
@@ -383,6 +386,18 @@ void Communicator::check_status() const {
     os << "b200ar: rank " << s.rank << " timed out waiting for rank " << s.peer << " (cta " << s.cta << ", epoch "
        << s.epoch << ", last seen " << s.seen << ", " << s.count << " CTA(s) affected); the communicator must be "
        << "reset() collectively";
+    throw CommTimeout(os.str());
+  }
+  if (s.code == kStatusBadEpoch) {
+    os << "b200ar: rank " << s.rank << " found flag " << s.seen << " from rank " << s.peer << " while waiting for "
+       << "epoch " << s.epoch << " (cta " << s.cta << "): the signal block holds data the protocol never writes "
+       << "(stale or corrupted); the communicator must be reset() collectively";
+    throw CommTimeout(os.str());
+  }
+  if (s.code == kStatusOutOfBounds) {
+    os << "b200ar: rank " << s.rank << " skipped a call whose " << (s.peer == 2u ? "Lamport" : "slot")
+       << " footprint (" << s.epoch << " bytes, low word) exceeds its buffer (" << s.seen
+       << " bytes, low word); the communicator must be reset() collectively";
     throw CommTimeout(os.str());
   }
   os << "b200ar: device reported error code " << s.code;

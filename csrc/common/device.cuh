@@ -235,8 +235,38 @@ B200AR_DEV bool cta_barrier(const CommCtx& c, int cta, uint32_t epoch) {
         }
       }
     }
+#if defined(B200AR_CHECKS)
+    // Checked builds: a flag further ahead than any peer can be means the
+    // signal block was overwritten; fail instead of trusting the data.
+    if (!fail && epoch_too_far(seen, epoch)) {
+      report_status(c.status, kStatusBadEpoch, c.rank, peer, cta, epoch, seen);
+      fail = 1;
+    }
+#endif
   }
   return __syncthreads_or(fail) == 0;
+}
+
+// Checked builds (-DB200AR_CHECKS): a kernel verifies on entry that the byte
+// range it is about to touch, [0, need), lies inside its buffer of `cap`
+// bytes. On failure it records kStatusOutOfBounds (peer = `what`, epoch and
+// seen = low words of need and cap) and the caller skips every access; peers
+// then time out at their next barrier. Without the flag this is `true`.
+B200AR_DEV bool range_ok(const CommCtx& c, int64_t need, int64_t cap, uint32_t what) {
+#if defined(B200AR_CHECKS)
+  if (need > cap) {
+    if (threadIdx.x == 0)
+      report_status(c.status, kStatusOutOfBounds, c.rank, what, blockIdx.x, static_cast<uint32_t>(need),
+                    static_cast<uint32_t>(cap));
+    return false;
+  }
+#else
+  (void)c;
+  (void)need;
+  (void)cap;
+  (void)what;
+#endif
+  return true;
 }
 
 }  // namespace b200ar

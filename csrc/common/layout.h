@@ -35,6 +35,9 @@ constexpr uint32_t kEpochsPerCall = 2;
 // Upper bound on output tiles of one fused GEMM + all-reduce call.
 constexpr int kMaxTiles = 4096;
 
+// Identifies a b200ar CPU segment ("b2ar").
+constexpr uint32_t kSegmentMagic = 0x72613262u;
+
 enum class DType : int { kFloat32 = 0, kFloat16 = 1, kBFloat16 = 2 };
 
 B200AR_HD int dtype_size(DType d) { return d == DType::kFloat32 ? 4 : 2; }
@@ -44,6 +47,9 @@ enum StatusCode : uint32_t {
   kStatusOk = 0,
   kStatusTimeout = 1,      // a peer did not arrive at a barrier before the deadline
   kStatusBadArgs = 2,      // a kernel found arguments it cannot serve
+  kStatusBadEpoch = 3,     // a peer's flag is further ahead than the protocol allows:
+                           // the signal block was overwritten (stale or foreign data)
+  kStatusOutOfBounds = 4,  // checked builds: an access range exceeded its buffer
 };
 
 // Error record. Lives in host-mapped pinned memory (GPU) or process memory
@@ -67,7 +73,16 @@ struct alignas(256) Signal {
   uint32_t gen;
   // CTAs of the current call that have finished (local only, reset by the last).
   uint32_t done;
-  uint32_t reserved[62];
+  // Segment header (CPU backend): written by the owner, checked by every peer
+  // when it maps the segment, so a wrong or corrupted exchanged name fails on
+  // the host instead of mapping foreign memory. The GPU path leaves it zero.
+  uint32_t magic;          // kSegmentMagic
+  uint32_t owner_rank;     // rank that created the segment
+  uint32_t world;          // world size it was created for
+  uint32_t slot_cap_lo;    // slot capacity in bytes (low / high word)
+  uint32_t slot_cap_hi;
+  uint32_t lamport_cap;    // Lamport capacity in bytes
+  uint32_t reserved[56];
   // flags[cta][src]: highest epoch that rank `src` reached in CTA `cta`.
   // Written remotely by rank `src`, read locally.
   uint32_t flags[kMaxCTAs][kMaxRanks];
@@ -85,6 +100,16 @@ B200AR_HD uint32_t epoch_of(uint32_t gen, uint32_t b) { return gen * kEpochsPerC
 
 // True once `seen` has reached `want` under wrap-around arithmetic.
 B200AR_HD bool epoch_reached(uint32_t seen, uint32_t want) { return static_cast<int32_t>(seen - want) >= 0; }
+
+// True if `seen` is further ahead of `want` than any peer can legitimately be.
+// A peer passes a barrier only after this rank arrived at it, so while this
+// rank waits for epoch e of a flag row the peer can have finished the current
+// call and arrived at the next barrier of that row: at most e + kEpochsPerCall
+// (one-barrier calls use epoch 2g + 1 of each call). Anything beyond is data
+// that the protocol never writes.
+B200AR_HD bool epoch_too_far(uint32_t seen, uint32_t want) {
+  return static_cast<int32_t>(seen - want) > static_cast<int32_t>(kEpochsPerCall);
+}
 
 // Start of part `i` when `total` items are split into `parts` nearly equal parts.
 B200AR_HD int64_t part_begin(int64_t total, int parts, int i) { return (total * i) / parts; }

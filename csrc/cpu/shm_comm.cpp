@@ -5,6 +5,7 @@
 #include <c10/util/Half.h>
 #include <fcntl.h>
 #include <sys/mman.h>
+#include <sys/stat.h>
 #include <unistd.h>
 
 #include <atomic>
@@ -53,6 +54,15 @@ inline void packet_store(char* p, const float* acc) {
   for (int i = 0; i < elems<T>(); ++i) e[i] = from_f<T>(acc[i]);
 }
 
+void write_header(Signal* sig, int rank, int world, int64_t slot_cap, int64_t lam_cap) {
+  sig->owner_rank = static_cast<uint32_t>(rank);
+  sig->world = static_cast<uint32_t>(world);
+  sig->slot_cap_lo = static_cast<uint32_t>(slot_cap & 0xffffffffu);
+  sig->slot_cap_hi = static_cast<uint32_t>(slot_cap >> 32);
+  sig->lamport_cap = static_cast<uint32_t>(lam_cap);
+  __atomic_store_n(&sig->magic, kSegmentMagic, __ATOMIC_RELEASE);
+}
+
 }  // namespace
 
 ShmComm::ShmComm(const std::string& prefix, int rank, int world, int64_t slot_capacity, int64_t lamport_capacity)
@@ -77,6 +87,7 @@ ShmComm::ShmComm(const std::string& prefix, int rank, int world, int64_t slot_ca
     throw std::runtime_error("mmap of shared segment failed");
   }
   std::memset(p, 0, sizeof(Signal));
+  write_header(static_cast<Signal*>(p), rank, world, slot_capacity, lamport_capacity);
   uint32_t* lam = reinterpret_cast<uint32_t*>(static_cast<char*>(p) + workspace_bytes(cap_));
   for (int64_t i = 0; i < lamport_bytes(lam_cap_, world) / 4; ++i) lam[i] = kLamportMarker;
   base_[rank] = static_cast<char*>(p);
@@ -95,9 +106,31 @@ void ShmComm::connect(const std::vector<std::string>& names) {
     if (i == rank_) continue;
     const int fd = shm_open(names[i].c_str(), O_RDWR, 0600);
     if (fd < 0) throw std::runtime_error("shm_open(" + names[i] + ") failed: " + std::strerror(errno));
+    // A segment of the wrong size would fault on access: check before mapping.
+    struct stat sb {};
+    if (fstat(fd, &sb) != 0 || static_cast<int64_t>(sb.st_size) != seg_bytes_) {
+      close(fd);
+      std::ostringstream os;
+      os << "b200ar(cpu): segment '" << names[i] << "' given for rank " << i << " has " << sb.st_size
+         << " bytes, expected " << seg_bytes_ << " (corrupted or mismatched handle exchange)";
+      throw std::runtime_error(os.str());
+    }
     void* p = mmap(nullptr, seg_bytes_, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
     close(fd);
     if (p == MAP_FAILED) throw std::runtime_error("mmap of peer segment failed");
+    const Signal* sig = static_cast<const Signal*>(p);
+    const int64_t cap = static_cast<int64_t>(sig->slot_cap_lo) | (static_cast<int64_t>(sig->slot_cap_hi) << 32);
+    if (__atomic_load_n(&sig->magic, __ATOMIC_ACQUIRE) != kSegmentMagic || sig->owner_rank != static_cast<uint32_t>(i) ||
+        sig->world != static_cast<uint32_t>(world_) || cap != cap_ || sig->lamport_cap != static_cast<uint32_t>(lam_cap_)) {
+      std::ostringstream os;
+      os << "b200ar(cpu): segment '" << names[i] << "' given for rank " << i << " does not match (magic 0x" << std::hex
+         << sig->magic << std::dec << ", owner " << sig->owner_rank << ", world " << sig->world << ", slot capacity "
+         << cap << "; expected rank " << i << ", world " << world_ << ", slot capacity " << cap_
+         << "): corrupted or mismatched handle exchange";
+      munmap(p, seg_bytes_);
+      throw std::runtime_error(os.str());
+    }
+    if (base_[i]) munmap(base_[i], seg_bytes_);  // re-connect: drop the old mapping
     base_[i] = static_cast<char*>(p);
     names_[i] = names[i];
   }
@@ -107,6 +140,7 @@ uint32_t ShmComm::generation() const { return ld_acquire(&reinterpret_cast<Signa
 
 void ShmComm::reset() {
   std::memset(base_[rank_], 0, sizeof(Signal));
+  write_header(reinterpret_cast<Signal*>(base_[rank_]), rank_, world_, cap_, lam_cap_);
   // Peers' packets of an aborted call may sit in the Lamport buffers: restore
   // the markers so the next Lamport call does not read stale data.
   uint32_t* lam = reinterpret_cast<uint32_t*>(base_[rank_] + workspace_bytes(cap_));
@@ -116,11 +150,28 @@ void ShmComm::reset() {
   skip_ = 0;
 }
 
+void ShmComm::inject_flag(int cta, int src, uint32_t value) {
+  B200AR_CHECK(cta >= 0 && cta < kMaxCTAs && src >= 0 && src < world_, "flag index out of range");
+  st_release(&reinterpret_cast<Signal*>(base_[rank_])->flags[cta][src], value);
+}
+
 bool ShmComm::barrier(int cta, uint32_t epoch) {
   Signal* self = reinterpret_cast<Signal*>(base_[rank_]);
   for (int p = 0; p < world_; ++p)
     st_release(&reinterpret_cast<Signal*>(base_[p])->flags[cta][rank_], epoch);
   const auto start = std::chrono::steady_clock::now();
+  auto fail = [&](uint32_t code, int p, uint32_t seen) {
+    if (status_.code == kStatusOk) {
+      status_.code = code;
+      status_.rank = rank_;
+      status_.peer = p;
+      status_.cta = cta;
+      status_.epoch = epoch;
+      status_.seen = seen;
+    }
+    ++status_.count;
+    return false;
+  };
   for (int p = 0; p < world_; ++p) {
     uint32_t seen;
     uint32_t spins = 0;
@@ -129,20 +180,10 @@ bool ShmComm::barrier(int cta, uint32_t epoch) {
         std::this_thread::yield();
         const auto ms =
             std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - start).count();
-        if (ms > timeout_ms_) {
-          if (status_.code == kStatusOk) {
-            status_.code = kStatusTimeout;
-            status_.rank = rank_;
-            status_.peer = p;
-            status_.cta = cta;
-            status_.epoch = epoch;
-            status_.seen = seen;
-          }
-          ++status_.count;
-          return false;
-        }
+        if (ms > timeout_ms_) return fail(kStatusTimeout, p, seen);
       }
     }
+    if (epoch_too_far(seen, epoch)) return fail(kStatusBadEpoch, p, seen);
   }
   return true;
 }
@@ -223,8 +264,13 @@ void ShmComm::run(const char* in, char* out, int64_t P, int variant, int G) {
   __atomic_store_n(&self->gen, gen + 1u, __ATOMIC_RELEASE);
   if (!ok) {
     std::ostringstream os;
-    os << "b200ar(cpu): rank " << status_.rank << " timed out waiting for rank " << status_.peer << " (cta "
-       << status_.cta << ", epoch " << status_.epoch << ", last seen " << status_.seen << ")";
+    if (status_.code == kStatusBadEpoch)
+      os << "b200ar(cpu): rank " << status_.rank << " found flag " << status_.seen << " from rank " << status_.peer
+         << " while waiting for epoch " << status_.epoch << " (cta " << status_.cta
+         << "): the signal block holds data the protocol never writes (stale or corrupted)";
+    else
+      os << "b200ar(cpu): rank " << status_.rank << " timed out waiting for rank " << status_.peer << " (cta "
+         << status_.cta << ", epoch " << status_.epoch << ", last seen " << status_.seen << ")";
     throw CommTimeout(os.str());
   }
 }

@@ -49,6 +49,9 @@ class ShmComm {
   // Skips the next `n` calls' barriers on this rank (host-side fault injection
   // for tests: the peers must time out).
   void inject_skip(int n) { skip_ = n; }
+  // Overwrites flags[cta][src] of this rank's own signal block with `value`
+  // (host-side fault injection for tests: a stale or foreign epoch).
+  void inject_flag(int cta, int src, uint32_t value);
 
  private:
   bool barrier(int cta, uint32_t epoch);

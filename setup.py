@@ -2,6 +2,11 @@
 
 Every CUDA source is compiled for sm_100a only (B200); the explicit -gencode
 flag keeps torch from adding its own architecture list.
+
+``B200AR_CHECKS=1 python setup.py build_ext --inplace`` builds the checked
+debug library ``b200ar/_C_checked*.so`` instead (device-side range and epoch
+checks that record errors in the status word; objects under build/checked).
+Importing b200ar with ``B200AR_CHECKS=1`` in the environment loads it.
 """
 
 import glob
@@ -27,13 +32,16 @@ def sources():
     return sorted(set(os.path.relpath(f, ROOT) for f in files))
 
 
+CHECKED = os.environ.get("B200AR_CHECKS") == "1"
+DEFINES = ["-DB200AR_CHECKS"] if CHECKED else []
+
 NVCC_FLAGS = ARCH + [
     "-O3",
     "-lineinfo",
     "-std=c++17",
     "--expt-relaxed-constexpr",
     "-Xptxas=-warn-spills",
-]
+] + DEFINES
 
 setup(
     name="b200ar",
@@ -41,12 +49,13 @@ setup(
     packages=["b200ar"],
     ext_modules=[
         CUDAExtension(
-            name="b200ar._C",
+            name="b200ar._C_checked" if CHECKED else "b200ar._C",
             sources=sources(),
             include_dirs=[os.path.join(ROOT, "csrc")],
-            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"] + DEFINES, "nvcc": NVCC_FLAGS},
             extra_link_args=["-lrt"],
         )
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+    options={"build": {"build_temp": os.path.join("build", "checked")}} if CHECKED else {},
 )
