@@ -21,6 +21,7 @@ Semantics are those of the reference, with these fixes:
 """
 
 from ._native import _C
+from .ipc import allocator_blocks_ipc
 
 init_custom_ar = _C.init_custom_ar
 all_reduce = _C.all_reduce
@@ -28,8 +29,23 @@ dispose = _C.dispose
 meta_size = _C.meta_size
 register_buffer = _C.register_buffer
 register_pcie_buffers = _C.register_pcie_buffers
-get_graph_buffer_ipc_meta = _C.get_graph_buffer_ipc_meta
 register_graph_buffers = _C.register_graph_buffers
+
+
+
+def get_graph_buffer_ipc_meta(fa: int):
+    """IPC handles (as byte lists) and offsets of the inputs captured since the
+    last registration. The error names the allocator setting when one makes
+    the captured tensors non-exportable."""
+    try:
+        return _C.get_graph_buffer_ipc_meta(fa)
+    except RuntimeError as e:
+        why = allocator_blocks_ipc()
+        if why is None:
+            raise
+        raise RuntimeError(f"cannot export the captured all-reduce inputs over CUDA IPC while {why} is set; "
+                           "unset it or capture with registered double buffers (register_pcie_buffers)") from e
+
 
 __all__ = [
     "init_custom_ar",

@@ -12,6 +12,7 @@ handle twice returns the same mapping), and helpers to exchange handles over a
 from __future__ import annotations
 
 import ctypes
+import os
 from typing import List, Optional
 
 import torch.distributed as dist
@@ -60,7 +61,7 @@ class CudaIPC:
         _C.ipc_memset(_as_int(ptr), int(value), int(count))
 
     def ipc_get_handle(self, ptr) -> cudaIpcMemHandle_t:
-        return cudaIpcMemHandle_t.from_bytes(_C.ipc_get_handle(_as_int(ptr)))
+        return cudaIpcMemHandle_t.from_bytes(export_handle(_as_int(ptr)))
 
     def ipc_open_handle(self, handle) -> ctypes.c_void_p:
         raw = handle.to_bytes() if isinstance(handle, cudaIpcMemHandle_t) else bytes(handle)
@@ -70,12 +71,45 @@ class CudaIPC:
         _C.ipc_close_handle(_as_int(ptr))
 
 
+def allocator_blocks_ipc() -> Optional[str]:
+    """Names the PyTorch allocator setting under which tensor memory cannot be
+    exported with ``cudaIpcGetMemHandle`` (``expandable_segments`` maps memory
+    with the virtual-memory API; the ``cudaMallocAsync`` backend allocates from
+    a stream-ordered pool), or None."""
+    for var in ("PYTORCH_CUDA_ALLOC_CONF", "PYTORCH_ALLOC_CONF"):
+        for item in os.environ.get(var, "").replace(";", ",").split(","):
+            key, _, value = item.partition(":")
+            key, value = key.strip().lower(), value.strip().lower()
+            if key == "expandable_segments" and value == "true":
+                return f"{var}=expandable_segments:True"
+            if key == "backend" and value == "cudamallocasync":
+                return f"{var}=backend:cudaMallocAsync"
+    return None
+
+
+def export_handle(ptr: int) -> bytes:
+    """``cudaIpcGetMemHandle`` of the allocation holding ``ptr``. When the
+    export fails under an allocator setting that makes tensor memory
+    non-exportable, the error names that setting and the way out."""
+    try:
+        return _C.ipc_get_handle(int(ptr))
+    except RuntimeError as e:
+        why = allocator_blocks_ipc()
+        if why is None:
+            raise
+        raise RuntimeError(
+            f"cannot export address {int(ptr):#x} over CUDA IPC while {why} is set: that allocator setting "
+            "gives memory cudaIpcGetMemHandle cannot export. Allocate registered buffers with "
+            "b200ar.ipc.CudaIPC().malloc (plain cudaMalloc), or unset the setting."
+        ) from e
+
+
 def exchange_buffers(ptr: int, group=None) -> List[int]:
     """All-gathers the IPC handle of this rank's allocation ``ptr`` and returns
     every rank's pointer as mapped in this process (own pointer at own rank)."""
     rank = dist.get_rank(group)
     world = dist.get_world_size(group)
-    handle = _C.ipc_get_handle(int(ptr))
+    handle = export_handle(ptr)
     handles: List[Optional[bytes]] = [None] * world
     dist.all_gather_object(handles, handle, group=group)
     out = []

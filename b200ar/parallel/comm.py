@@ -293,7 +293,16 @@ class CustomAllreduce:
     def register_graph_buffers(self) -> None:
         if self._comm is None:
             return
-        handles, offsets = self._comm.graph_buffer_meta()
+        try:
+            handles, offsets = self._comm.graph_buffer_meta()
+        except RuntimeError as e:
+            from ..ipc import allocator_blocks_ipc
+
+            why = allocator_blocks_ipc()
+            if why is None:
+                raise
+            raise RuntimeError(f"cannot export the inputs captured for variant='registered' while {why} is set; "
+                               "use the slot variants in graphs (no registration needed) or unset it") from e
         meta: List[Optional[tuple]] = [None] * self.world
         dist.all_gather_object(meta, (handles, offsets), group=self.group)
         self._comm.register_graph_buffers([m[0] for m in meta], [m[1] for m in meta])

@@ -105,3 +105,27 @@ def test_slot_bytes_formulas():
     assert _C.variant_slot_bytes(VARIANTS["twoshot"], 16 * 10, 4) == 5 * 3 * 16
     assert _C.lamport_bytes(1024, 8) == 3 * 8 * 1024
     assert _C.gemm_ar_slot_bytes(128, 256, 2) == 3 * 1 * 128 * 256 * 2
+
+
+def test_allocator_settings_that_block_ipc(monkeypatch):
+    from b200ar import ipc
+
+    for var in ("PYTORCH_CUDA_ALLOC_CONF", "PYTORCH_ALLOC_CONF"):
+        monkeypatch.delenv(var, raising=False)
+    assert ipc.allocator_blocks_ipc() is None
+    monkeypatch.setenv("PYTORCH_CUDA_ALLOC_CONF", "max_split_size_mb:128,expandable_segments:True")
+    assert "expandable_segments" in ipc.allocator_blocks_ipc()
+    monkeypatch.setenv("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:False")
+    assert ipc.allocator_blocks_ipc() is None
+    monkeypatch.setenv("PYTORCH_ALLOC_CONF", "backend:cudaMallocAsync")
+    assert "cudaMallocAsync" in ipc.allocator_blocks_ipc()
+
+    def failing_export(ptr):
+        raise RuntimeError("CUDA error: invalid argument")
+
+    monkeypatch.setattr(ipc._C, "ipc_get_handle", failing_export)
+    with pytest.raises(RuntimeError, match="CudaIPC\\(\\).malloc"):
+        ipc.export_handle(0x1000)
+    monkeypatch.delenv("PYTORCH_ALLOC_CONF")
+    with pytest.raises(RuntimeError, match="^CUDA error"):  # no setting to blame: the original error
+        ipc.export_handle(0x1000)
