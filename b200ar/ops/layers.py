@@ -21,6 +21,9 @@ from .._native import _C
 def rmsnorm(x: torch.Tensor, gamma: torch.Tensor, eps: float = 1e-5, out=None) -> torch.Tensor:
     if out is None:
         out = torch.empty_like(x)
+    if torch.compiler.is_compiling():  # traced: the dispatcher op of the same kernel
+        torch.ops.b200ar.rmsnorm(x.contiguous(), gamma, float(eps), out)
+        return out
     _C.rmsnorm(x.contiguous(), gamma, out, float(eps))
     return out
 
@@ -96,6 +99,9 @@ def silu_mul(gate_up, out=None):
     rows, two_i = gate_up.shape
     if out is None:
         out = torch.empty(rows, two_i // 2, dtype=gate_up.dtype, device=gate_up.device)
+    if torch.compiler.is_compiling():
+        torch.ops.b200ar.silu_mul(gate_up, out)
+        return out
     _C.silu_mul(gate_up, out)
     return out
 

@@ -76,6 +76,12 @@ class CustomAllreduce:
         self.set_selector(sel.load_table(self.world, self.cfg.selector_path or None))
 
     # ------------------------------------------------------------------ setup
+    @property
+    def handle(self) -> int:
+        """Native communicator handle for the ``torch.ops.b200ar`` operators
+        (0 for the CPU backend or after ``close()``)."""
+        return self._handle if self._comm is not None else 0
+
     def _init_cpu(self) -> None:
         token = [uuid.uuid4().hex[:12] if self.rank == 0 else None]
         dist.broadcast_object_list(token, src=dist.get_global_rank(self.group, 0) if self.group else 0,
@@ -105,6 +111,7 @@ class CustomAllreduce:
             self._peer_ptrs = ptrs
             self._rank_data = torch.empty(self.cfg.rank_data_bytes, dtype=torch.uint8, device=self.device)
             self._comm = _C.Comm(ptrs, self._rank_data, self.rank)
+            self._handle = int(self._comm.ptr)
             sig = int(_C.SIGNAL_BYTES)
             self._comm.register_slots(
                 [p + sig for p in ptrs], [p + sig + self.slot_capacity for p in ptrs], self.slot_capacity
@@ -171,6 +178,11 @@ class CustomAllreduce:
         if out is None:
             out = torch.empty_like(inp)
         v = sel.variant_id(variant if variant != "auto" else self.cfg.variant)
+        if self._comm is not None and torch.compiler.is_compiling():
+            # Traced by torch.compile: one dispatcher op, no host-side fallback
+            # (messages above the NCCL crossover run the two-shot kernel).
+            torch.ops.b200ar.all_reduce(self._handle, inp, out, v, int(ctas))
+            return out
         if self._comm is None:
             # The CPU emulation implements the slot variants and the Lamport one-shot.
             cpu_ok = (sel.VARIANTS["oneshot_push"], sel.VARIANTS["oneshot_pull"], sel.VARIANTS["twoshot"],
@@ -212,6 +224,10 @@ class CustomAllreduce:
             y = zf * torch.rsqrt(zf.pow(2).mean(-1, keepdim=True) + eps) * gamma.float()
             residual_out.copy_(zb)
             out.copy_(y.to(out.dtype))
+            return out, residual_out
+        if torch.compiler.is_compiling():
+            torch.ops.b200ar.all_reduce_residual_rmsnorm(self._handle, x, residual, gamma, float(eps), out,
+                                                         residual_out, sel.variant_id(variant), int(ctas))
             return out, residual_out
         self._comm.ar_rmsnorm(x, residual, gamma, out, residual_out, float(eps), sel.variant_id(variant), int(ctas))
         return out, residual_out

@@ -116,3 +116,44 @@ def test_fused_rmsnorm_world_one():
         torch.testing.assert_close(y.float(), y_ref.float(), atol=2e-2, rtol=1e-2)
     comm.close()
     dist.destroy_process_group()
+
+
+def test_torch_ops_match_eager_paths():
+    """torch.ops.b200ar (direct and traced by torch.compile) gives bitwise the
+    results of the pybind entry points: same kernels, same streams."""
+    import torch.distributed as dist
+
+    from dist_util import free_port
+
+    from b200ar import CustomAllreduce
+    from b200ar.ops.layers import rmsnorm, silu_mul
+
+    if not dist.is_initialized():
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{free_port()}", rank=0, world_size=1)
+    comm = CustomAllreduce(device=torch.device("cuda", 0), max_size=8 << 20)
+    assert comm.handle != 0
+    H = 4096
+    x = torch.randn(33, H, device="cuda").to(torch.bfloat16)
+    res = torch.randn(33, H, device="cuda").to(torch.bfloat16)
+    gamma = (1 + 0.01 * torch.randn(H, device="cuda")).to(torch.bfloat16)
+
+    def layer(x, res, g):
+        s = comm.all_reduce(x)
+        y, z = comm.all_reduce_residual_rmsnorm(s, res, g, 1e-5)
+        return silu_mul(torch.cat([rmsnorm(y, g, 1e-5), z], dim=1))
+
+    ref = layer(x, res, gamma)
+    s = torch.empty_like(x)
+    torch.ops.b200ar.all_reduce(comm.handle, x, s)
+    y = torch.empty_like(x)
+    z = torch.empty_like(x)
+    torch.ops.b200ar.all_reduce_residual_rmsnorm(comm.handle, s, res, gamma, 1e-5, y, z)
+    y_ref, z_ref = comm.all_reduce_residual_rmsnorm(x, res, gamma, 1e-5)
+    torch.cuda.synchronize()
+    assert torch.equal(s, x) and torch.equal(y, y_ref) and torch.equal(z, z_ref)
+    torch._dynamo.reset()
+    out = torch.compile(layer, fullgraph=True, backend="aot_eager")(x, res, gamma)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    comm.close()
+    dist.destroy_process_group()
