@@ -84,3 +84,29 @@ def percentile(values: Sequence[float], q: float) -> float:
 def geomean(values: Sequence[float]) -> float:
     v = [x for x in values if x > 0]
     return math.exp(sum(math.log(x) for x in v) / len(v)) if v else float("nan")
+
+
+# Measured NVLink peer-copy bandwidth per direction per GPU on B200 HGX boxes
+# (GB/s); the denominator of the all-reduce bandwidth fraction.
+NVLINK_GBS = 770.0
+
+
+def latency_stats(samples_us: Sequence[float]) -> Dict[str, float]:
+    """p10 / p50 / p90 / max of per-call latencies (already the max over
+    ranks of each call), rounded to ns."""
+    return {
+        "p10": round(percentile(samples_us, 10), 3),
+        "p50": round(percentile(samples_us, 50), 3),
+        "p90": round(percentile(samples_us, 90), 3),
+        "max": round(max(samples_us), 3) if samples_us else float("nan"),
+    }
+
+
+def allreduce_bandwidth(nbytes: int, world: int, us: float, link_gbs: float = NVLINK_GBS) -> Dict[str, float]:
+    """nccl-tests conventions: algbw = S / t; busbw = algbw * 2 (N - 1) / N,
+    the per-GPU link traffic of a bandwidth-optimal all-reduce. The fraction
+    relates busbw to one GPU's NVLink bandwidth per direction."""
+    algbw = nbytes / (us * 1e-6) / 1e9
+    busbw = algbw * 2 * (world - 1) / world if world > 1 else 0.0
+    return {"algbw_gbs": round(algbw, 1), "busbw_gbs": round(busbw, 1),
+            "busbw_frac_of_nvlink": round(busbw / link_gbs, 3)}

@@ -232,7 +232,8 @@ def capture_graphs(fn_by_size, sz_list):
 def run(args):
     sys.path.insert(0, ROOT)
     from b200ar.utils.clocks import ClockSampler
-    from b200ar.utils.timing import EventTimer, L2Flusher, geomean, max_over_ranks, percentile
+    from b200ar.utils.timing import (EventTimer, L2Flusher, allreduce_bandwidth, geomean, latency_stats,
+                                     max_over_ranks, percentile)
     from b200ar.parallel.selector import crossover_bytes
 
     rank, world, local, gloo = init_dist(args.gpus)
@@ -299,7 +300,9 @@ def run(args):
     launches = arm.launches() - launches0 + args.steps * len(graphs)
     total_ms = max_over_ranks([t0.elapsed_time(t1)], dev)[0]
     times = timer.times_ms()
-    p50 = {key: percentile(max_over_ranks(vals, dev), 50) * 1e3 for key, vals in times.items()}  # µs
+    per_call = {key: [v * 1e3 for v in max_over_ranks(vals, dev)] for key, vals in times.items()}  # µs
+    p50 = {key: percentile(v, 50) for key, v in per_call.items()}
+    stats = {key: latency_stats(v) for key, v in per_call.items()}
     clocks = sampler.summary() if local == 0 else {}
 
     # ---- end to end through the public API: pinned H2D, all-reduce, D2H ----
@@ -340,8 +343,11 @@ def run(args):
             row["nccl_eager_p50_us"] = round(p50[f"nccl_eager/{s}"], 3)
             if nccl_graphs:
                 row["nccl_graph_p50_us"] = round(p50[f"nccl_graph/{s}"], 3)
+        row["eager_us"] = stats[f"eager/{s}"]
+        if graphs:
+            row["graph_us"] = stats[f"graph/{s}"]
         if world > 1:
-            row["busbw_gbs"] = round(2 * (world - 1) / world * s / (p50[f"eager/{s}"] * 1e-6) / 1e9, 1)
+            row.update(allreduce_bandwidth(s, world, p50[f"eager/{s}"]))
         sweep.append(row)
         for mode in ("eager", "graph"):
             if f"{mode}/{s}" in p50 and f"nccl_{mode}/{s}" in p50:

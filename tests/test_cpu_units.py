@@ -129,3 +129,41 @@ def test_allocator_settings_that_block_ipc(monkeypatch):
     monkeypatch.delenv("PYTORCH_ALLOC_CONF")
     with pytest.raises(RuntimeError, match="^CUDA error"):  # no setting to blame: the original error
         ipc.export_handle(0x1000)
+
+
+def test_latency_stats_and_bandwidth():
+    from b200ar.utils.timing import NVLINK_GBS, allreduce_bandwidth, latency_stats
+
+    st = latency_stats([float(v) for v in range(1, 12)])  # 1..11 us
+    assert st == {"p10": 2.0, "p50": 6.0, "p90": 10.0, "max": 11.0}
+    bw = allreduce_bandwidth(1 << 30, 8, 1e6 * (1 << 30) / 700e9)  # 1 GiB in the time of 700 GB/s algbw
+    assert bw["algbw_gbs"] == 700.0
+    assert bw["busbw_gbs"] == round(700.0 * 14 / 8, 1)
+    assert bw["busbw_frac_of_nvlink"] == round(700.0 * 14 / 8 / NVLINK_GBS, 3)
+    assert allreduce_bandwidth(4096, 1, 1.0)["busbw_gbs"] == 0.0
+
+
+def test_render_md_tables(tmp_path):
+    import importlib.util
+    import os
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("render_md", os.path.join(root, "bench", "render_md.py"))
+    rm = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(rm)
+    ours = {"impl": "b200ar", "n_gpus": 2, "metric": "m", "value": 1.0, "unit": "us",
+            "sweep": [{"bytes": 4096, "variant": "lamport", "eager_p50_us": 10.0, "graph_p50_us": 8.0,
+                       "eager_us": {"p10": 9.0, "p50": 10.0, "p90": 12.0, "max": 20.0},
+                       "nccl_eager_p50_us": 20.0, "busbw_gbs": 0.4, "busbw_frac_of_nvlink": 0.001}],
+            "crossover_bytes": {"eager": None}, "clocks": {"sm_mhz": 1965, "sm_max_mhz": 1965, "reasons": []}}
+    ref = {"impl": "reference", "sweep": [{"bytes": 4096, "eager_p50_us": 30.0}]}
+    md = rm.render(ours, ref)
+    assert "| 4096 | lamport | 10.00 (9.00-12.00) | 8.00 | 20.00 | 2.00x | 0.4 | 0.00 | 30.00 | 3.00x |" in md
+    assert "crossover" in md and "1965 of 1965" in md
+    assert "unavailable" in rm.render({"impl": "reference", "unavailable": "odd world"})
+    p = tmp_path / "r.json"
+    p.write_text("NCCL version banner\n" + json.dumps(ours) + "\n")
+    assert len(rm.load_lines(str(p))) == 1
+    # The committed TP8 result renders (older lines carry fewer fields).
+    committed = rm.load_lines(os.path.join(root, "profiles", "bench_tp8.json"))
+    assert committed and "| 268435456 |" in rm.render(committed[-1])
