@@ -172,7 +172,12 @@ class CustomAllreduce:
     # ------------------------------------------------------------ collectives
     def all_reduce(self, inp: torch.Tensor, out: Optional[torch.Tensor] = None, variant="auto",
                    ctas: int = 0) -> torch.Tensor:
-        """Returns the elementwise sum of ``inp`` over all ranks (``out`` may alias ``inp``)."""
+        """Returns the elementwise sum of ``inp`` over all ranks (``out`` may alias ``inp``).
+
+        Contiguous float32/float16/bfloat16 tensors of a multiple of 16 bytes
+        on a 16-byte boundary run on the b200ar kernels (or NCCL above the
+        measured crossover). Other tensors go to NCCL when an NCCL group is
+        available, else through a zero-padded contiguous copy."""
         if self.closed:
             raise RuntimeError("communicator is closed")
         if out is None:
@@ -183,6 +188,10 @@ class CustomAllreduce:
             # (messages above the NCCL crossover run the two-shot kernel).
             torch.ops.b200ar.all_reduce(self._handle, inp, out, v, int(ctas))
             return out
+        if not (self.supports(inp) and self.supports(out)):
+            if self._comm is not None and self.nccl_group is not None:
+                return self._nccl(inp, out)
+            return self._staged(inp, out, variant, ctas)
         if self._comm is None:
             # The CPU emulation implements the slot variants and the Lamport one-shot.
             cpu_ok = (sel.VARIANTS["oneshot_push"], sel.VARIANTS["oneshot_pull"], sel.VARIANTS["twoshot"],
@@ -192,7 +201,7 @@ class CustomAllreduce:
                 v = sel.VARIANTS["auto"]
             self._shm.all_reduce(inp, out, v, ctas)
             return out
-        if not self.supports(inp) or not self.supports(out) or v == sel.VARIANTS["nccl"]:
+        if v == sel.VARIANTS["nccl"]:
             return self._nccl(inp, out)
         launched = self._comm.all_reduce(inp, out, v, ctas)
         if launched == sel.VARIANTS["nccl"]:
@@ -276,6 +285,22 @@ class CustomAllreduce:
         else:
             full.copy_(x_shard)
         return linear(full, w, out=out)
+
+    def _staged(self, inp: torch.Tensor, out: torch.Tensor, variant, ctas: int) -> torch.Tensor:
+        """Serves a tensor the kernels cannot take as it is (size not a
+        multiple of 16 bytes, misaligned or strided) through a zero-padded
+        contiguous copy when no NCCL group is available."""
+        if inp.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+            raise TypeError(f"b200ar all-reduce supports float32, float16 and bfloat16, not {inp.dtype}")
+        if out.dtype != inp.dtype or out.numel() != inp.numel():
+            raise ValueError("input and output must have the same dtype and number of elements")
+        n = inp.numel()
+        per16 = 16 // inp.element_size()
+        buf = torch.zeros((n + per16 - 1) // per16 * per16, dtype=inp.dtype, device=inp.device)
+        buf[:n].copy_(inp.reshape(-1))
+        res = self.all_reduce(buf, variant=variant, ctas=ctas)
+        out.copy_(res[:n].reshape(out.shape))
+        return out
 
     def _nccl(self, inp: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         if self.nccl_group is None:

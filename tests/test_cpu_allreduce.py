@@ -207,3 +207,32 @@ def _dead_peer_entry(rank, world):
     # Skip the final dist.barrier() of the harness for the departed rank: both
     # ranks meet here once rank 0 observed the timeout.
     dist.barrier()
+
+
+def _ragged(rank, world):
+    # Sizes that are not a multiple of 16 bytes, misaligned views and strided
+    # tensors go through a padded staging copy; results stay exact.
+    from b200ar import CustomAllreduce
+
+    comm = CustomAllreduce(device="cpu", max_size=1 << 20)
+    for dtype in (torch.float32, torch.bfloat16):
+        for numel in (1, 7, 13, 1025):
+            g = torch.Generator().manual_seed(numel + 31 * rank)
+            base = (torch.rand(3 * numel + 3, generator=g) * 2 - 1).to(dtype)
+            for name, x in (("plain", base[:numel].clone()), ("misaligned", base[1:1 + numel]),
+                            ("strided", base[::3][:numel])):
+                xs = [None] * world
+                dist.all_gather_object(xs, x.clone())
+                ref = sum(t.float() for t in xs).to(dtype)
+                out = comm.all_reduce(x)
+                assert torch.equal(out, ref), (dtype, numel, name)
+                y = torch.empty(3 * numel, dtype=dtype)[::3]  # strided output
+                comm.all_reduce(x, out=y)
+                assert torch.equal(y, ref), (dtype, numel, name, "strided out")
+    with pytest.raises(TypeError):
+        comm.all_reduce(torch.ones(5, dtype=torch.int32))
+    comm.close()
+
+
+def test_ragged_misaligned_strided():
+    run_ranks(_ragged, 2)
