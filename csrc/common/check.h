@@ -9,6 +9,8 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
+#include <cstdint>
 #include <sstream>
 #include <stdexcept>
 #include <string>
@@ -44,3 +46,28 @@ struct CommTimeout : public std::runtime_error {
       throw std::invalid_argument(b200ar_os__.str());                 \
     }                                                                 \
   } while (0)
+
+namespace b200ar {
+
+// Runs a set-up step once per CUDA device (devices 0-63), e.g. raising a
+// kernel's dynamic shared-memory limit with cudaFuncSetAttribute, which is a
+// per-device attribute: a process that drives several GPUs needs it on each.
+// Two threads may both run the step for one device; the steps used here are
+// idempotent.
+class PerDeviceOnce {
+ public:
+  template <typename Fn>
+  void operator()(Fn&& fn) {
+    int dev = 0;
+    B200AR_CUDA(cudaGetDevice(&dev));
+    const uint64_t bit = 1ull << (static_cast<unsigned>(dev) & 63u);
+    if (done_.load(std::memory_order_acquire) & bit) return;
+    fn();
+    done_.fetch_or(bit, std::memory_order_acq_rel);
+  }
+
+ private:
+  std::atomic<uint64_t> done_{0};
+};
+
+}  // namespace b200ar

@@ -130,12 +130,11 @@ void ag_gemm(Communicator& comm, cudaStream_t stream, const void* x_shard, const
     for (int p = 0; p < world; ++p)
       ga.maps[sl][p] = make_tmap_bf16_2d(comm.slot_ptr(sl, p), rows_per_rank, K, K, kSliceRows, gemm::BK);
   auto kern = gemm::gemm_kernel<gemm::StoreC, GatherA>;
-  static bool attr = false;
-  if (!attr) {
+  static PerDeviceOnce smem_attr;
+  smem_attr([&] {
     B200AR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(gemm::smem_bytes<gemm::StoreC>())));
-    attr = true;
-  }
+  });
   kern<<<gemm_grid(s, 0), gemm::THREADS, gemm::smem_bytes<gemm::StoreC>(), stream>>>(ga, tb, s, epi, err);
   B200AR_CUDA(cudaGetLastError());
   comm.count_launch();

@@ -237,12 +237,11 @@ void gemm_allreduce(Communicator& comm, cudaStream_t stream, const void* A, cons
   epi.world = comm.world();
   epi.tiles_per_owner = (s.tiles_m * s.tiles_n + comm.world() - 1) / comm.world();
   auto kern = gemm::gemm_kernel<ArEpi>;
-  static bool attr = false;
-  if (!attr) {
+  static PerDeviceOnce smem_attr;
+  smem_attr([&] {
     B200AR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(gemm::smem_bytes<ArEpi>())));
-    attr = true;
-  }
+  });
   // Every CTA must be resident (ranks wait on each other's CTAs): one per SM.
   int dev = 0, sms = 0;
   B200AR_CUDA(cudaGetDevice(&dev));

@@ -88,12 +88,11 @@ void gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int6
   const CUtensorMap tb = make_tmap_bf16_2d(B, N, K, K, gemm::BN, gemm::BK);
   gemm::StoreC epi{static_cast<__nv_bfloat16*>(C), N};
   auto kern = gemm::gemm_kernel<gemm::StoreC>;
-  static bool attr = false;
-  if (!attr) {
+  static PerDeviceOnce smem_attr;
+  smem_attr([&] {
     B200AR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(gemm::smem_bytes<gemm::StoreC>())));
-    attr = true;
-  }
+  });
   kern<<<gemm_grid(s, max_ctas), gemm::THREADS, gemm::smem_bytes<gemm::StoreC>(), stream>>>(ta, tb, s, epi, err);
   B200AR_CUDA(cudaGetLastError());
 }

@@ -250,11 +250,10 @@ void launch_skinny(const void* x, const void* w, void* out, float* partials, uns
   a.kblocks = static_cast<int>((K + SBK - 1) / SBK);
   a.splits = splits;
   auto kern = skinny_kernel<MP>;
-  static bool attr = false;
-  if (!attr) {
+  static PerDeviceOnce smem_attr;
+  smem_attr([&] {
     B200AR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM)));
-    attr = true;
-  }
+  });
   kern<<<a.nblocks * splits, STHREADS, C::SMEM, stream>>>(tw, tx, a, err);
   B200AR_CUDA(cudaGetLastError());
 }

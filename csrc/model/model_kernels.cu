@@ -413,12 +413,11 @@ void decode_attention(const void* q, const void* k_cache, const void* v_cache, c
   const int group = hq / hkv;
   B200AR_CHECK(group <= kAttnMaxGroup, "GQA group size must be at most 16");
   B200AR_CHECK(splits >= 1, "splits must be positive");
-  static bool attr = false;
-  if (!attr) {
+  static PerDeviceOnce smem_attr;
+  smem_attr([&] {
     B200AR_CUDA(cudaFuncSetAttribute(attn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(kAttnSmem)));
-    attr = true;
-  }
+  });
   const dim3 grid(static_cast<unsigned>(batch), hkv, splits);
   attn_partial_kernel<<<grid, kAttnThreads, kAttnSmem, s>>>(
       static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k_cache),
