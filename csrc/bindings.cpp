@@ -155,6 +155,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     return std::make_tuple(reinterpret_cast<int64_t>(b), s);
   });
 
+  // ---- rank-data arena bookkeeping (host only; exposed for tests) ----
+  m.attr("RANK_DATA_BYTES") = static_cast<int64_t>(sizeof(RankData));
+  py::class_<RankDataArena>(m, "RankDataArena")
+      .def(py::init([](int64_t base, int64_t bytes) { return RankDataArena(reinterpret_cast<void*>(base), bytes); }),
+           py::arg("base"), py::arg("bytes"))
+      .def_property_readonly("capacity", &RankDataArena::capacity)
+      .def_property_readonly("used", &RankDataArena::used)
+      .def_property_readonly("remaining", &RankDataArena::remaining)
+      .def("fits", &RankDataArena::fits)
+      .def("peek", [](const RankDataArena& a, int64_t k) { return reinterpret_cast<int64_t>(a.peek(k)); })
+      .def("take", [](RankDataArena& a, int64_t n) { return reinterpret_cast<int64_t>(a.take(n)); });
+
   // ---- idiomatic communicator ----
   py::class_<Communicator>(m, "Comm")
       .def(py::init([](const std::vector<int64_t>& signals, at::Tensor& rank_data, int rank) {

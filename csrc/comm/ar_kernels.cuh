@@ -24,12 +24,6 @@ namespace b200ar {
 
 constexpr int kArThreads = 512;
 
-// Peer pointers of registered user buffers, stored in device memory so that
-// CUDA-graph captures can reference a slot that is filled after capture.
-struct alignas(16) RankData {
-  const void* ptrs[kMaxRanks];
-};
-
 struct ArArgs {
   CommCtx ctx;
   char* slot[2][kMaxRanks];  // base of slot s on every rank (peer mappings)

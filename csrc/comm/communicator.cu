@@ -117,8 +117,7 @@ Communicator::Communicator(const std::vector<int64_t>& signals, void* rank_data,
     B200AR_CHECK(signals[i] % 256 == 0, "signal block of rank " << i << " must be 256-byte aligned");
     signals_[i] = reinterpret_cast<Signal*>(signals[i]);
   }
-  arena_next_ = reinterpret_cast<RankData*>(rank_data);
-  arena_end_ = arena_next_ + (rank_data ? rank_data_bytes / static_cast<int64_t>(sizeof(RankData)) : 0);
+  arena_ = RankDataArena(rank_data, rank_data_bytes);
   B200AR_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&status_host_), sizeof(Status), cudaHostAllocMapped));
   std::memset(status_host_, 0, sizeof(Status));
   B200AR_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&status_dev_), status_host_, 0));
@@ -138,13 +137,6 @@ char* Communicator::open_ipc_handle(const std::string& handle) {
   char* p = IpcRegistry::get().open(handle);
   opened_.push_back(p);
   return p;
-}
-
-RankData* Communicator::arena_take(size_t n) {
-  if (arena_next_ + n > arena_end_) throw std::runtime_error("Rank data buffer overflow");
-  RankData* r = arena_next_;
-  arena_next_ += n;
-  return r;
 }
 
 void Communicator::register_slots(const std::vector<int64_t>& ptrs0, const std::vector<int64_t>& ptrs1,
@@ -171,7 +163,7 @@ void Communicator::register_slots(const std::vector<int64_t>& ptrs0, const std::
   // so that a caller staging into them can use the registered path.
   for (int s = 0; s < 2; ++s) {
     std::vector<int64_t> ptrs(s == 0 ? ptrs0 : ptrs1);
-    if (arena_next_ + 1 <= arena_end_) register_buffer(ptrs);
+    if (arena_.fits(1)) register_buffer(ptrs);
   }
 }
 
@@ -189,9 +181,14 @@ void Communicator::register_lamport(const std::vector<int64_t>& ptrs, int64_t ca
 
 void Communicator::register_buffer(const std::vector<int64_t>& ptrs) {
   B200AR_CHECK(static_cast<int>(ptrs.size()) == world_, "need one buffer pointer per rank");
+  // Kernels captured since the last register_graph_buffers() reference the
+  // next arena records by position: taking one now would shift them.
+  B200AR_CHECK(graph_pending_.empty(), "register_graph_buffers() must follow the capture of "
+                                           << graph_pending_.size()
+                                           << " registered all-reduce(s) before another buffer is registered");
   RankData rd{};
   for (int i = 0; i < world_; ++i) rd.ptrs[i] = reinterpret_cast<const void*>(ptrs[i]);
-  RankData* d = arena_take(1);
+  RankData* d = arena_.take(1);
   B200AR_CUDA(cudaMemcpy(d, &rd, sizeof(RankData), cudaMemcpyHostToDevice));
   buffers_[reinterpret_cast<const void*>(ptrs[rank_])] = d;
 }
@@ -232,7 +229,7 @@ void Communicator::register_graph_buffers(const std::vector<std::string>& handle
       }
     }
   }
-  RankData* d = arena_take(n);
+  RankData* d = arena_.take(static_cast<int64_t>(n));
   B200AR_CUDA(cudaMemcpy(d, rds.data(), n * sizeof(RankData), cudaMemcpyHostToDevice));
   graph_pending_.clear();
 }
@@ -347,8 +344,7 @@ LaunchInfo Communicator::allreduce(cudaStream_t stream, const void* in, void* ou
 #endif
   if (li.variant == kRegistered) {
     if (capturing) {
-      if (arena_next_ + graph_pending_.size() + 1 > arena_end_) throw std::runtime_error("Rank data buffer overflow");
-      a.rd = arena_next_ + graph_pending_.size();
+      a.rd = arena_.peek(static_cast<int64_t>(graph_pending_.size()));  // throws when the arena is full
       graph_pending_.push_back(in);
     } else {
       if (!registered_input)

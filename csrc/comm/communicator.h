@@ -25,6 +25,7 @@
 
 #include "../common/check.h"
 #include "../common/layout.h"
+#include "arena.h"
 
 namespace b200ar {
 
@@ -157,13 +158,10 @@ class Communicator {
   char* slot_ptr(int slot, int r) const { return slots_[slot][r]; }
 
  private:
-  RankData* arena_take(size_t n);
-
   int rank_ = 0;
   int world_ = 0;
   Signal* signals_[kMaxRanks] = {};
-  RankData* arena_next_ = nullptr;
-  RankData* arena_end_ = nullptr;
+  RankDataArena arena_;
 
   std::unordered_map<const void*, RankData*> buffers_;
   std::vector<const void*> graph_pending_;

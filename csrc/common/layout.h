@@ -65,6 +65,14 @@ struct alignas(64) Status {
   uint32_t pad[9];
 };
 
+// Peer pointers of one registered buffer (entry i = rank i's copy as mapped
+// in this process). Kept in a device-memory arena so that a CUDA-graph capture
+// can reference a record that is filled after capture (the reference's
+// RankData, pcie_allreduce.cu:58-61).
+struct alignas(16) RankData {
+  const void* ptrs[kMaxRanks];
+};
+
 // Per-rank signal block, placed at offset 0 of each rank's shared workspace.
 // It must be zero-initialised before first use (like the reference's
 // memset of its Signal buffer, test_pcie_ar.py:36).

@@ -167,3 +167,26 @@ def test_render_md_tables(tmp_path):
     # The committed TP8 result renders (older lines carry fewer fields).
     committed = rm.load_lines(os.path.join(root, "profiles", "bench_tp8.json"))
     assert committed and "| 268435456 |" in rm.render(committed[-1])
+
+
+def test_rank_data_arena_bookkeeping():
+    from b200ar import _C
+
+    rec = int(_C.RANK_DATA_BYTES)
+    assert rec == 8 * 8  # one pointer per rank, kMaxRanks = 8
+    base = 0x7F0000000000  # addresses only: the arena never dereferences them
+    a = _C.RankDataArena(base, 10 * rec + rec // 2)
+    assert (a.capacity, a.used, a.remaining) == (10, 0, 10)
+    assert a.take(3) == base
+    # Capture reserves records by position without taking them.
+    assert a.peek(0) == base + 3 * rec and a.peek(2) == base + 5 * rec
+    assert a.take(1) == base + 3 * rec
+    assert a.fits(6) and not a.fits(7) and not a.fits(-1)
+    with pytest.raises(RuntimeError, match="overflow: 7 record"):
+        a.take(7)
+    assert a.used == 4  # a failed take leaves the arena unchanged
+    with pytest.raises(RuntimeError, match="overflow"):
+        a.peek(6)
+    assert a.take(6) == base + 4 * rec and a.remaining == 0
+    empty = _C.RankDataArena(0, 1 << 20)  # no buffer: nothing fits
+    assert empty.capacity == 0 and not empty.fits(1)
