@@ -59,7 +59,8 @@ class TPLlamaDecoder:
         cfg: model shape.
         batch: decode batch size (static: the step is graph-captured).
         max_len: KV cache capacity in tokens.
-        seed: weights are drawn from ``seed + 1000 * rank``.
+        seed: sharded weights are drawn from ``seed + 1000 * rank``; the
+            replicated RMSNorm weights from one seed shared by all ranks.
     """
 
     def __init__(self, comm, cfg: LlamaConfig, batch: int, max_len: int, seed: int = 0):
@@ -77,13 +78,16 @@ class TPLlamaDecoder:
         self.batch = batch
         self.max_len = max_len
         d, H = cfg.head_dim, cfg.hidden
+        # Sharded weights differ per rank; the RMSNorm weights are replicated
+        # (like the residual stream), so every rank draws them from one seed.
         g = torch.Generator(device=self.device).manual_seed(seed + 1000 * self.rank)
+        g_rep = torch.Generator(device=self.device).manual_seed(seed + 999_983)
 
         def rnd(*shape):
             return (cfg.init_std * torch.randn(*shape, generator=g, device=self.device)).to(torch.bfloat16)
 
         def gamma():
-            return (1 + 0.01 * torch.randn(H, generator=g, device=self.device)).to(torch.bfloat16)
+            return (1 + 0.01 * torch.randn(H, generator=g_rep, device=self.device)).to(torch.bfloat16)
 
         self.layers = []
         for _ in range(cfg.layers):
@@ -227,7 +231,8 @@ class ReferenceDecoder:
             m.k_cache[i][ar, idx] = k
             m.v_cache[i][ar, idx] = qkv[:, m.hq + m.hkv:]
             # Attention over the first seq_len positions (the same length for the whole batch here).
-            n = int(m.seq_len[0]) if not torch.cuda.is_current_stream_capturing() else self._cap_len
+            capturing = m.device.type == "cuda" and torch.cuda.is_current_stream_capturing()
+            n = self._cap_len if capturing else int(m.seq_len[0])
             kk = m.k_cache[i][:, :n].transpose(1, 2)  # [B, hkv, n, d]
             vv = m.v_cache[i][:, :n].transpose(1, 2)
             a = torch.nn.functional.scaled_dot_product_attention(q.unsqueeze(2), kk, vv, enable_gqa=True)

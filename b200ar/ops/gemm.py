@@ -2,7 +2,8 @@
 
 ``linear(x, w)`` computes ``x @ w.T`` for ``x [M, K]`` and ``w [N, K]`` (the
 ``nn.Linear`` weight layout) with the hand-written sm_100a kernel in
-``csrc/gemm``; fp32 accumulation, bf16 output.
+``csrc/gemm``; fp32 accumulation, bf16 output. CPU tensors (the plumbing
+backend) use the fp32 reference product.
 """
 
 from __future__ import annotations
@@ -66,6 +67,9 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
     if out is None:
         out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
     out2 = out.view(m, n)
+    if x.device.type == "cpu":  # plumbing backend: fp32 reference math, never a CUDA fallback
+        out2.copy_((x2.float() @ w.float().t()).to(out2.dtype))
+        return out.view(*shp[:-1], n)
     if skinny is None:
         skinny = m <= 128
     if skinny:

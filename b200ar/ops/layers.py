@@ -6,6 +6,10 @@ each with a plain-PyTorch fp32 reference used by the tests.
 * ``rope_kv``            rotate q and k (rotate-half convention), write k and v into the KV cache
 * ``decode_attention``   GQA decode attention over the KV cache (split-KV, online softmax)
 * ``silu_mul``           silu(gate) * up
+
+CUDA tensors always run the sm_100a kernels. CPU tensors (the gloo/shared-memory
+plumbing backend, used to test tensor-parallel logic without a GPU) run the
+fp32 reference math of each op; no CUDA call falls back to it.
 """
 
 from __future__ import annotations
@@ -21,6 +25,9 @@ from .._native import _C
 def rmsnorm(x: torch.Tensor, gamma: torch.Tensor, eps: float = 1e-5, out=None) -> torch.Tensor:
     if out is None:
         out = torch.empty_like(x)
+    if x.device.type == "cpu":
+        out.copy_(ref_rmsnorm(x, gamma, eps))
+        return out
     if torch.compiler.is_compiling():  # traced: the dispatcher op of the same kernel
         torch.ops.b200ar.rmsnorm(x.contiguous(), gamma, float(eps), out)
         return out
@@ -46,6 +53,14 @@ class RotaryTable:
 
 def rope_kv(qkv, pos, rot: RotaryTable, q_out, k_cache, v_cache, hq: int, hkv: int) -> None:
     """qkv [B, (hq + 2 hkv) * d] -> q_out [B, hq, d]; k, v into caches [B, L, hkv, d] at ``pos``."""
+    if qkv.device.type == "cpu":
+        b, d = qkv.shape[0], rot.head_dim
+        x = qkv.view(b, hq + 2 * hkv, d)
+        q_out.copy_(ref_rope(x[:, :hq], pos, rot).to(q_out.dtype))
+        rows, idx = torch.arange(b), pos.long()
+        k_cache[rows, idx] = ref_rope(x[:, hq:hq + hkv], pos, rot).to(k_cache.dtype)
+        v_cache[rows, idx] = x[:, hq + hkv:].to(v_cache.dtype)
+        return
     _C.rope_kv(qkv, pos, rot.cos, rot.sin, q_out, k_cache, v_cache, hq, hkv, rot.head_dim)
 
 
@@ -69,6 +84,9 @@ def decode_attention(q, k_cache, v_cache, seq_len, hq: int, hkv: int, out=None, 
     b = q.shape[0]
     if out is None:
         out = torch.empty(b, hq * 128, dtype=q.dtype, device=q.device)
+    if q.device.type == "cpu":
+        out.copy_(ref_decode_attention(q, k_cache, v_cache, seq_len, hq, hkv).to(out.dtype))
+        return out
     if splits <= 0:
         splits = _C.attention_splits(b, hkv, k_cache.shape[1])
     key = (q.device.index or 0, b * hq * splits, b * hkv)
@@ -99,6 +117,9 @@ def silu_mul(gate_up, out=None):
     rows, two_i = gate_up.shape
     if out is None:
         out = torch.empty(rows, two_i // 2, dtype=gate_up.dtype, device=gate_up.device)
+    if gate_up.device.type == "cpu":
+        out.copy_(ref_silu_mul(gate_up))
+        return out
     if torch.compiler.is_compiling():
         torch.ops.b200ar.silu_mul(gate_up, out)
         return out

@@ -280,7 +280,11 @@ class CustomAllreduce:
             self._comm.ag_gemm(x_shard.contiguous(), w, out, error_word(x_shard.device))
             return out
         full = torch.empty(rows * self.world, k, dtype=x_shard.dtype, device=x_shard.device)
-        if self.world > 1:
+        if self.world > 1 and self._comm is None:  # CPU backend: gather over the bootstrap group
+            parts = [torch.empty_like(x_shard) for _ in range(self.world)]
+            dist.all_gather(parts, x_shard.contiguous(), group=self.group)
+            torch.cat(parts, dim=0, out=full)
+        elif self.world > 1:
             dist.all_gather_into_tensor(full, x_shard.contiguous(), group=self.nccl_group)
         else:
             full.copy_(x_shard)
