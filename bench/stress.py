@@ -17,8 +17,12 @@ PASS/FAIL per rank 0; the process exits non-zero on any failure.
   t11 cuda_graph_decode  capture 61 x (AR, copy, mul, mul, AR), replay 200
   t12 random_sizes       --random-iters calls, sizes uniform in 1 KB .. 64 MB,
                          random variants, oracle check every 1000 calls
+                         (--max-random-bytes, --check-every)
 
     python -m torch.distributed.run --nproc-per-node N bench/stress.py [--random-iters 100000]
+
+With ``--device cpu`` the same scenarios run on CPU ranks (gloo bootstrap +
+the shared-memory backend); the two CUDA-graph scenarios are skipped there.
 """
 
 from __future__ import annotations
@@ -44,15 +48,29 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--random-iters", type=int, default=100000)
     ap.add_argument("--only", default="")
+    ap.add_argument("--device", choices=["cuda", "cpu"], default="cuda")
+    ap.add_argument("--max-random-bytes", type=int, default=64 << 20)
+    ap.add_argument("--check-every", type=int, default=1000)
     args = ap.parse_args()
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
-    torch.cuda.set_device(local)
-    dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    gloo = dist.new_group(backend="gloo")
-    dev = torch.device("cuda", local)
-    comm = CustomAllreduce(group=gloo, device=dev, nccl_group=dist.group.WORLD, max_size=64 << 20)
+    on_gpu = args.device == "cuda"
+    if on_gpu:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        gloo = dist.new_group(backend="gloo")
+        dev = torch.device("cuda", local)
+        comm = CustomAllreduce(group=gloo, device=dev, nccl_group=dist.group.WORLD, max_size=64 << 20)
+    else:
+        dist.init_process_group("gloo")
+        gloo = dist.group.WORLD
+        dev = torch.device("cpu")
+        comm = CustomAllreduce(group=gloo, device=dev, max_size=max(args.max_random_bytes, 1 << 20))
+
+    def sync():
+        if on_gpu:
+            sync()
     ws = world
     tri = ws * (ws + 1) / 2.0
     results = {}
@@ -74,7 +92,7 @@ def main():
         t0 = time.perf_counter()
         for _ in range(10000):
             ar(x, out)
-        torch.cuda.synchronize()
+        sync()
         el = time.perf_counter() - t0
         check("rapid_fire", bool((out.float() - tri).abs().max() < 0.5), f"{el / 10000 * 1e6:.1f} us/call host")
 
@@ -99,7 +117,7 @@ def main():
         for i in range(5000):
             x = torch.full((1, HIDDEN), float(rank + 1) + i * 0.001, dtype=torch.bfloat16, device=dev)
             out = ar(x)
-        torch.cuda.synchronize()
+        sync()
         last = sum(float(r + 1) + 4999 * 0.001 for r in range(ws))
         check("back_to_back", bool((out.float() - last).abs().max() < 1.0))
 
@@ -133,7 +151,7 @@ def main():
                 scratch.mul_(1.0 / tri)
                 scratch.mul_(float(rank + 1))
                 ar(scratch, out)
-        torch.cuda.synchronize()
+        sync()
         el = time.perf_counter() - t0
         check("decode_step", bool((out.float() - tri).abs().max() < 1.0), f"{el / 50 * 1e3:.2f} ms/step host")
 
@@ -163,7 +181,7 @@ def main():
         with torch.cuda.stream(s):
             fn()
         torch.cuda.current_stream().wait_stream(s)
-        torch.cuda.synchronize()
+        sync()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             fn()
@@ -181,7 +199,7 @@ def main():
         for _ in range(500):
             gi.fill_(float(rank + 1))
             g.replay()
-        torch.cuda.synchronize()
+        sync()
         check("cuda_graph", bool((go.float() - tri).abs().max() < 0.5))
 
     def t11():
@@ -201,20 +219,20 @@ def main():
         for _ in range(200):
             gi.fill_(float(rank + 1))
             g.replay()
-        torch.cuda.synchronize()
+        sync()
         check("cuda_graph_decode", bool((go.float() - tri).abs().max() < 1.0))
 
     def t12():
         gen = torch.Generator().manual_seed(2024)
         variants = ["auto", "auto", "lamport", "oneshot_push", "oneshot_pull", "twoshot"]
-        big = torch.empty(32 << 20, dtype=torch.bfloat16, device=dev)  # 64 MB
+        big = torch.empty(args.max_random_bytes // 2, dtype=torch.bfloat16, device=dev)
         big.uniform_(-1, 1, generator=torch.Generator(device=dev).manual_seed(rank))
         out = torch.empty_like(big)
         ok = True
         checked = 0
         t0 = time.perf_counter()
         for i in range(args.random_iters):
-            nbytes = int(torch.randint(1 << 10, (64 << 20) + 1, (1,), generator=gen)) // 16 * 16
+            nbytes = int(torch.randint(1 << 10, args.max_random_bytes + 1, (1,), generator=gen)) // 16 * 16
             v = variants[int(torch.randint(len(variants), (1,), generator=gen))]
             if v == "lamport" and nbytes > comm.lamport_capacity:
                 v = "auto"
@@ -222,20 +240,25 @@ def main():
                 v = "auto"
             n = nbytes // 2
             ar(big[:n], out[:n], variant=v)
-            if i % 1000 == 999:
-                torch.cuda.synchronize()
+            if i % args.check_every == args.check_every - 1:
+                sync()
                 ref = big[:n].float()
                 dist.all_reduce(ref)
                 ok &= bool((out[:n].float() - ref).abs().max() <= 2e-2 * ws)
                 checked += 1
-        torch.cuda.synchronize()
+        sync()
         comm.check()
         el = time.perf_counter() - t0
-        check("random_sizes", ok, f"{args.random_iters} calls, {checked} oracle checks, {el:.1f} s")
+        check("random_sizes", ok, f"{args.random_iters} calls up to {args.max_random_bytes} B, {checked} oracle "
+                                  f"checks, {el:.1f} s")
 
     tests = [t1, t2, t3, t4, t5, t6, t7, t8, t9, t10, t11, t12]
     for t in tests:
         if args.only and t.__name__ not in args.only.split(","):
+            continue
+        if not on_gpu and t in (t10, t11):
+            if rank == 0:
+                print(f"  {t.__name__:<22s} SKIP (CUDA graphs need a GPU)", flush=True)
             continue
         dist.barrier()
         try:
@@ -247,7 +270,7 @@ def main():
     ok = all(results.values())
     if rank == 0:
         print(f"\n{'ALL STRESS TESTS PASSED' if ok else 'SOME STRESS TESTS FAILED'}", flush=True)
-    torch.cuda.synchronize()
+    sync()
     dist.barrier(group=gloo)
     sys.stdout.flush()
     os._exit(0 if ok else 1)
