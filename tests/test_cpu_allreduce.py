@@ -53,7 +53,7 @@ def _dtypes_sizes(rank, world):
     comm.close()
 
 
-@pytest.mark.parametrize("world", [2, 3, 4])
+@pytest.mark.parametrize("world", [2, 3, 4, 6])
 def test_dtypes_sizes_variants(world):
     run_ranks(_dtypes_sizes, world)
 
