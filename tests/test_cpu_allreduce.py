@@ -10,7 +10,7 @@ from dist_util import run_ranks
 VARIANTS = ["oneshot_push", "oneshot_pull", "twoshot", "lamport"]
 
 
-def _baseline_config1(rank, world):
+def _bf16_1024x1024_fp32_oracle(rank, world):
     # Benchmark configuration: bf16 [1024, 1024] ~ N(0, 1) seeded 1234 + rank, fp32 oracle, atol 2e-2.
     from b200ar import CustomAllreduce
 
@@ -30,8 +30,8 @@ def _baseline_config1(rank, world):
     comm.close()
 
 
-def test_baseline_config1_gloo_ws2():
-    run_ranks(_baseline_config1, 2)
+def test_bf16_1024x1024_fp32_oracle_gloo_ws2():
+    run_ranks(_bf16_1024x1024_fp32_oracle, 2)
 
 
 def _dtypes_sizes(rank, world):
