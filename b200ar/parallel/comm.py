@@ -169,6 +169,29 @@ class CustomAllreduce:
             and t.is_contiguous()
         )
 
+    # --------------------------------------------- serving-engine interface
+    @property
+    def disabled(self) -> bool:
+        return self.closed
+
+    def should_custom_ar(self, inp: torch.Tensor) -> bool:
+        """True when b200ar's own kernels serve ``inp`` (the interface of the
+        custom all-reduce wrappers in vLLM / SGLang): a supported dtype and
+        layout, within ``max_size``, and below the measured NCCL crossover."""
+        if self.closed or not self.supports(inp):
+            return False
+        nbytes = inp.numel() * inp.element_size()
+        if nbytes > self.cfg.max_size:
+            return False
+        return self.plan(nbytes)[0] != "nccl"
+
+    def custom_all_reduce(self, inp: torch.Tensor) -> Optional[torch.Tensor]:
+        """Out-of-place all-reduce if ``should_custom_ar(inp)``, else None (the
+        caller then uses its NCCL path), as in those wrappers."""
+        if not self.should_custom_ar(inp):
+            return None
+        return self.all_reduce(inp)
+
     # ------------------------------------------------------------ collectives
     def all_reduce(self, inp: torch.Tensor, out: Optional[torch.Tensor] = None, variant="auto",
                    ctas: int = 0) -> torch.Tensor:

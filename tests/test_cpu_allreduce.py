@@ -236,3 +236,25 @@ def _ragged(rank, world):
 
 def test_ragged_misaligned_strided():
     run_ranks(_ragged, 2)
+
+
+def _engine_interface(rank, world):
+    from b200ar import CustomAllreduce
+
+    comm = CustomAllreduce(device="cpu", max_size=1 << 16)
+    x = torch.full((1024,), float(rank + 1))
+    assert not comm.disabled
+    assert comm.should_custom_ar(x)
+    out = comm.custom_all_reduce(x)
+    assert out is not None and out.data_ptr() != x.data_ptr()
+    assert torch.all(out == sum(r + 1 for r in range(world)))
+    big = torch.zeros((1 << 16) // 4 + 4)  # above max_size: the caller's NCCL path
+    assert not comm.should_custom_ar(big) and comm.custom_all_reduce(big) is None
+    assert not comm.should_custom_ar(torch.zeros(5, dtype=torch.int32))
+    assert not comm.should_custom_ar(torch.zeros(7, dtype=torch.bfloat16))  # 14 bytes
+    comm.close()
+    assert comm.disabled and not comm.should_custom_ar(x)
+
+
+def test_serving_engine_interface():
+    run_ranks(_engine_interface, 2)
