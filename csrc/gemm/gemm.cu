@@ -8,6 +8,7 @@
 #include <unordered_map>
 
 #include "../common/check.h"
+#include "../common/trace.h"
 #include "gemm.cuh"
 #include "gemm_api.h"
 
@@ -82,6 +83,7 @@ int gemm_grid(const gemm::Shape& s, int max_ctas) {
 
 void gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int* err, cudaStream_t stream,
                int max_ctas) {
+  const TraceRange trace("b200ar::gemm_bf16");
   const gemm::Shape s = gemm_shape(M, N, K);
   B200AR_CHECK(N % 8 == 0 && reinterpret_cast<uintptr_t>(C) % 16 == 0, "C must have 16-byte aligned rows");
   const gemm::TmapA ta{make_tmap_bf16_2d(A, M, K, K, gemm::BM, gemm::BK)};

@@ -19,6 +19,7 @@
 #include <stdexcept>
 
 #include "../common/check.h"
+#include "../common/trace.h"
 #include "gemm_api.h"
 #include "tcgen05.cuh"
 
@@ -270,6 +271,7 @@ int skinny_splits(int64_t N, int64_t K, int sms) {
 
 void gemm_skinny(const void* x, const void* w, void* out, float* partials, unsigned* counters, int64_t M, int64_t N,
                  int64_t K, int splits, int* err, cudaStream_t stream) {
+  const TraceRange trace("b200ar::gemm_skinny");
   B200AR_CHECK(M >= 1 && M <= SBM, "skinny GEMM serves 1 <= M <= 128, got " << M);
   B200AR_CHECK(K % 8 == 0 && N % 8 == 0, "K and N must be multiples of 8");
   B200AR_CHECK(splits >= 1 && (splits == 1 || (partials && counters)), "split-K needs partials and counters");

@@ -18,6 +18,7 @@
 #include <stdexcept>
 
 #include "../common/check.h"
+#include "../common/trace.h"
 #include "../common/device.cuh"
 #include "model.h"
 
@@ -377,6 +378,7 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloa
 }  // namespace
 
 void rmsnorm(const void* x, const void* gamma, void* y, int64_t rows, int64_t hidden, float eps, cudaStream_t s) {
+  const TraceRange trace("b200ar::rmsnorm");
   B200AR_CHECK(hidden % 8 == 0, "hidden must be a multiple of 8");
   const int threads = static_cast<int>(std::min<int64_t>(512, std::max<int64_t>(32, (hidden / 8 + 31) / 32 * 32)));
   rmsnorm_kernel<<<static_cast<unsigned>(rows), threads, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
@@ -388,6 +390,7 @@ void rmsnorm(const void* x, const void* gamma, void* y, int64_t rows, int64_t hi
 
 void rope_kv(const void* qkv, const int* pos, const float* cos_t, const float* sin_t, void* q_out, void* k_cache,
              void* v_cache, int64_t batch, int hq, int hkv, int head_dim, int max_len, cudaStream_t s) {
+  const TraceRange trace("b200ar::rope_kv");
   B200AR_CHECK(head_dim % 2 == 0 && head_dim <= 1024, "bad head dim");
   rope_kv_kernel<<<dim3(static_cast<unsigned>(batch), hq + hkv), head_dim / 2, 0, s>>>(
       static_cast<const __nv_bfloat16*>(qkv), pos, cos_t, sin_t, static_cast<__nv_bfloat16*>(q_out),
@@ -408,6 +411,7 @@ int attention_splits(int64_t batch, int hkv, int max_len) {
 void decode_attention(const void* q, const void* k_cache, const void* v_cache, const int* seq_len, void* out,
                       float* part_acc, float* part_ml, unsigned* done_count, int64_t batch, int hq, int hkv,
                       int head_dim, int max_len, int splits, float scale, cudaStream_t s) {
+  const TraceRange trace("b200ar::decode_attention");
   B200AR_CHECK(head_dim == kHeadDim, "decode attention is built for head_dim 128");
   B200AR_CHECK(hkv > 0 && hq % hkv == 0, "query heads must be a multiple of KV heads");
   const int group = hq / hkv;
@@ -427,6 +431,7 @@ void decode_attention(const void* q, const void* k_cache, const void* v_cache, c
 }
 
 void silu_mul(const void* gate_up, void* y, int64_t rows, int64_t inter, cudaStream_t s) {
+  const TraceRange trace("b200ar::silu_mul");
   B200AR_CHECK(inter % 8 == 0, "intermediate size must be a multiple of 8");
   const int64_t items = rows * inter / 8;
   const int blocks = static_cast<int>(std::min<int64_t>((items + 255) / 256, 4 * 148));
