@@ -54,6 +54,7 @@ class CustomAllreduce:
             nccl_group = dist.group.WORLD
         self.nccl_group = nccl_group
         self.closed = False
+        self._handle = 0  # native communicator address (CUDA backend), for torch.ops.b200ar
         self._peer_ptrs: List[int] = []
         self._ws_ptr = 0
         self.nvls = None
@@ -80,7 +81,7 @@ class CustomAllreduce:
     def handle(self) -> int:
         """Native communicator handle for the ``torch.ops.b200ar`` operators
         (0 for the CPU backend or after ``close()``)."""
-        return self._handle if self._comm is not None else 0
+        return self._handle
 
     def _init_cpu(self) -> None:
         token = [uuid.uuid4().hex[:12] if self.rank == 0 else None]
@@ -206,7 +207,7 @@ class CustomAllreduce:
         if out is None:
             out = torch.empty_like(inp)
         v = sel.variant_id(variant if variant != "auto" else self.cfg.variant)
-        if self._comm is not None and torch.compiler.is_compiling():
+        if torch.compiler.is_compiling() and self._handle:
             # Traced by torch.compile: one dispatcher op, no host-side fallback
             # (messages above the NCCL crossover run the two-shot kernel).
             torch.ops.b200ar.all_reduce(self._handle, inp, out, v, int(ctas))
@@ -249,6 +250,10 @@ class CustomAllreduce:
             out = torch.empty_like(x)
         if residual_out is None:
             residual_out = torch.empty_like(residual)
+        if torch.compiler.is_compiling() and self._handle:
+            torch.ops.b200ar.all_reduce_residual_rmsnorm(self._handle, x, residual, gamma, float(eps), out,
+                                                         residual_out, sel.variant_id(variant), int(ctas))
+            return out, residual_out
         if self._comm is None:
             z = self.all_reduce(x.float().contiguous()) + residual.float()
             zb = z.to(residual.dtype)
@@ -256,10 +261,6 @@ class CustomAllreduce:
             y = zf * torch.rsqrt(zf.pow(2).mean(-1, keepdim=True) + eps) * gamma.float()
             residual_out.copy_(zb)
             out.copy_(y.to(out.dtype))
-            return out, residual_out
-        if torch.compiler.is_compiling():
-            torch.ops.b200ar.all_reduce_residual_rmsnorm(self._handle, x, residual, gamma, float(eps), out,
-                                                         residual_out, sel.variant_id(variant), int(ctas))
             return out, residual_out
         self._comm.ar_rmsnorm(x, residual, gamma, out, residual_out, float(eps), sel.variant_id(variant), int(ctas))
         return out, residual_out
@@ -415,6 +416,7 @@ class CustomAllreduce:
         if self._comm is not None:
             del self._comm
             self._comm = None
+            self._handle = 0
             for i, p in enumerate(self._peer_ptrs):
                 if i != self.rank:
                     _C.ipc_close_handle(p)
