@@ -120,6 +120,23 @@ def crossover_bytes(measurements: Sequence[dict], ours: str = "custom", theirs: 
     return cross
 
 
+def parity_band(measurements: Sequence[dict], ours: str = "custom", theirs: str = "nccl", lo: float = 0.9,
+                hi: float = 1.1) -> List[int]:
+    """Sizes whose speedup t_theirs / t_ours lies in [lo, hi]: the reference
+    benchmark's crossover marker (bench_crossover.py:207, 232), reported next
+    to ``crossover_bytes``."""
+    best: Dict[Tuple[int, str], float] = {}
+    for m in measurements:
+        key = (int(m["bytes"]), m["impl"])
+        best[key] = min(best.get(key, float("inf")), float(m["us"]))
+    out = []
+    for s in sorted({k[0] for k in best}):
+        a, b = best.get((s, ours)), best.get((s, theirs))
+        if a and b is not None and lo <= b / a <= hi:
+            out.append(s)
+    return out
+
+
 def save_tables(path: str, tables: Dict[int, List[Entry]], meta: Optional[dict] = None) -> None:
     data = {"meta": meta or {}, "tables": {str(w): [list(e) for e in t] for w, t in sorted(tables.items())}}
     with open(path, "w") as f:

@@ -234,7 +234,7 @@ def run(args):
     from b200ar.utils.clocks import ClockSampler
     from b200ar.utils.timing import (EventTimer, L2Flusher, allreduce_bandwidth, geomean, latency_stats,
                                      max_over_ranks, percentile)
-    from b200ar.parallel.selector import crossover_bytes
+    from b200ar.parallel.selector import crossover_bytes, parity_band
 
     rank, world, local, gloo = init_dist(args.gpus)
     dev = torch.device("cuda", local)
@@ -385,6 +385,7 @@ def run(args):
     }
     if with_nccl:
         result["crossover_bytes"] = {m: crossover_bytes(r) for m, r in cross_rows.items() if r}
+        result["crossover_band_bytes"] = {m: parity_band(r) for m, r in cross_rows.items() if r}
     if e2e:
         result["e2e"] = e2e
     arm.close()

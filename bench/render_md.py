@@ -77,6 +77,10 @@ def render(result: dict, reference: Optional[dict] = None) -> str:
     if cross:
         lines += ["", "NCCL crossover (first size from which NCCL is faster): " +
                   ", ".join(f"{k} {v if v is not None else 'none'}" for k, v in cross.items())]
+    band = result.get("crossover_band_bytes")
+    if band:
+        lines += ["NCCL / ours within [0.9, 1.1] (the reference's crossover marker): " +
+                  "; ".join(f"{k} {', '.join(str(b) for b in v) or 'none'}" for k, v in band.items())]
     clocks = result.get("clocks")
     if clocks:
         lines += ["", f"SM clock under load: {clocks.get('sm_mhz')} of {clocks.get('sm_max_mhz')} MHz, "

@@ -190,3 +190,12 @@ def test_rank_data_arena_bookkeeping():
     assert a.take(6) == base + 4 * rec and a.remaining == 0
     empty = _C.RankDataArena(0, 1 << 20)  # no buffer: nothing fits
     assert empty.capacity == 0 and not empty.fits(1)
+
+
+def test_parity_band_matches_reference_definition():
+    from b200ar.parallel.selector import parity_band
+
+    rows = []
+    for s, (ours, nccl) in {1: (10, 30), 2: (10, 10.5), 4: (10, 9.2), 8: (10, 8.0), 16: (10, 10.0)}.items():
+        rows += [{"bytes": s, "impl": "custom", "us": ours}, {"bytes": s, "impl": "nccl", "us": nccl}]
+    assert parity_band(rows) == [2, 4, 16]
