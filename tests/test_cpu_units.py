@@ -199,3 +199,14 @@ def test_parity_band_matches_reference_definition():
     for s, (ours, nccl) in {1: (10, 30), 2: (10, 10.5), 4: (10, 9.2), 8: (10, 8.0), 16: (10, 10.0)}.items():
         rows += [{"bytes": s, "impl": "custom", "us": ours}, {"bytes": s, "impl": "nccl", "us": nccl}]
     assert parity_band(rows) == [2, 4, 16]
+
+
+def test_info_cli(capsys):
+    from b200ar.__main__ import main
+
+    assert main(["--json"]) == 0
+    info = json.loads(capsys.readouterr().out)
+    assert info["library"].startswith("_C") and set(info["selector"]) == {"2", "4", "8"}
+    assert info["config"]["max_size"] > 0
+    assert main([]) == 0
+    assert "selector, 8 ranks" in capsys.readouterr().out
