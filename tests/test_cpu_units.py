@@ -210,3 +210,26 @@ def test_info_cli(capsys):
     assert info["config"]["max_size"] > 0
     assert main([]) == 0
     assert "selector, 8 ranks" in capsys.readouterr().out
+
+
+def test_attention_split_rule():
+    from b200ar import _C
+
+    for batch, hkv, max_len in ((1, 1, 2065), (8, 1, 2065), (32, 1, 2065), (64, 1, 2065), (4, 8, 4096),
+                                (1, 1, 100), (512, 8, 2065)):
+        s = _C.attention_splits(batch, hkv, max_len)
+        assert 1 <= s <= 64
+        # One wave of at most 3 CTAs per SM on 148 SMs (when the batch allows it).
+        assert batch * hkv * s <= max(3 * 148, batch * hkv)
+        # At least two 64-token chunks of cache per split.
+        assert s == 1 or max_len // s >= 128
+    assert _C.attention_splits(64, 1, 2065) == 6 and _C.attention_splits(1, 1, 2065) == 16
+
+
+def test_skinny_split_rule():
+    from b200ar import _C
+
+    for n, k in ((1280, 8192), (7168, 8192), (8192, 3584), (8192, 1024), (128, 256)):
+        s = _C.skinny_splits(n, k, 148)
+        assert 1 <= s <= 16
+        assert s == 1 or ((n + 127) // 128) * s <= 148
