@@ -27,6 +27,14 @@ from b200ar.models.llama import LlamaConfig, ReferenceDecoder, TPLlamaDecoder  #
 from b200ar.utils.timing import EventTimer, max_over_ranks, percentile  # noqa: E402
 
 
+def step_bytes(model) -> int:
+    """Bytes one decode step must read from HBM on this rank: every weight
+    matrix once, plus the KV cache of every layer up to the current length."""
+    w = sum(t.numel() * t.element_size() for L in model.layers for t in L.values())
+    kv_per_token = 2 * model.hkv * model.cfg.head_dim * 2 * len(model.layers)
+    return w + int(model.seq_len.max().item()) * kv_per_token * model.batch
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--batches", default="1,8,32,64")
@@ -46,13 +54,17 @@ def main():
     dev = torch.device("cuda", local)
     comm = CustomAllreduce(group=gloo, device=dev, nccl_group=dist.group.WORLD, max_size=16 << 20)
     cfg = LlamaConfig.llama3_70b_slice(args.layers)
+    peaks = {}
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pk):
+        peaks = json.load(open(pk))
     for B in (int(b) for b in args.batches.split(",")):
         model = TPLlamaDecoder(comm, cfg, batch=B, max_len=args.context + args.warmup + 2 * args.iters + 8)
         model.prefill_random(args.context)
         model.set_input((torch.randn(B, cfg.hidden, device=dev)).to(torch.bfloat16))
         ours = model.capture()
         ref = ReferenceDecoder(model).capture()
-        res = {"batch": B, "world": world, "layers": cfg.layers}
+        res = {"batch": B, "world": world, "layers": cfg.layers, "hbm_bytes_per_step": step_bytes(model)}
         for name, g in (("b200ar", ours), ("torch_nccl", ref)):
             timer = EventTimer(pool=2 * args.iters)
             for it in range(args.warmup + args.iters):
@@ -65,6 +77,12 @@ def main():
             res[f"{name}_ms_per_step"] = round(ms, 4)
             res[f"{name}_tokens_per_s"] = round(B / (ms * 1e-3), 1)
         res["speedup"] = round(res["torch_nccl_ms_per_step"] / res["b200ar_ms_per_step"], 3)
+        if peaks.get("hbm_gbs"):
+            # Weight and KV streaming at the measured copy bandwidth (a lower
+            # bound that ignores the all-reduces and launch gaps).
+            bound_ms = res["hbm_bytes_per_step"] / (peaks["hbm_gbs"] * 1e9) * 1e3
+            res["hbm_bound_ms"] = round(bound_ms, 4)
+            res["b200ar_frac_of_hbm_bound"] = round(bound_ms / res["b200ar_ms_per_step"], 3)
         if rank == 0:
             print(json.dumps(res), flush=True)
         del model, ours, ref
