@@ -74,3 +74,29 @@ def _linear_collectives(rank, world):
 @pytest.mark.parametrize("world", [1, 2])
 def test_linear_collectives_cpu(world):
     run_ranks(_linear_collectives, world)
+
+
+def _step_bytes(rank, world):
+    import importlib.util
+    import os
+
+    from b200ar import CustomAllreduce
+    from b200ar.models.llama import LlamaConfig, TPLlamaDecoder
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("decoder_bench", os.path.join(root, "bench", "decoder_bench.py"))
+    db = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(db)
+    comm = CustomAllreduce(device="cpu", max_size=1 << 20)
+    cfg = LlamaConfig(hidden=256, heads=4, kv_heads=1, head_dim=128, intermediate=512, layers=2)
+    m = TPLlamaDecoder(comm, cfg, batch=2, max_len=32)
+    m.prefill_random(10)
+    H, d = 256, 128
+    weights = 2 * 2 * ((4 + 2) * d * H + H * 4 * d + 2 * 512 * H + H * 512 + 2 * H)  # 2 layers, bf16
+    kv = 11 * (2 * 1 * d * 2 * 2) * 2  # seq_len 11, k and v, 2 layers, batch 2
+    assert db.step_bytes(m) == weights + kv
+    comm.close()
+
+
+def test_decoder_bench_step_bytes():
+    run_ranks(_step_bytes, 1)
