@@ -233,3 +233,23 @@ def test_skinny_split_rule():
         s = _C.skinny_splits(n, k, 148)
         assert 1 <= s <= 16
         assert s == 1 or ((n + 127) // 128) * s <= 148
+
+
+def test_reference_import_names_resolve_to_b200ar():
+    import os
+    import subprocess
+    import sys
+
+    import b200ar.shim
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = ("import pcie_allreduce, cuda_ipc\n"
+            "from pcie_allreduce.cuda_ipc import CudaIPC\n"
+            "import b200ar.compat as c\n"
+            "assert pcie_allreduce.all_reduce is c.all_reduce and cuda_ipc.CudaIPC is CudaIPC\n"
+            "assert sorted(pcie_allreduce.__all__) == sorted(c.__all__)\n"
+            "assert pcie_allreduce.meta_size() == c.meta_size() > 0\n"
+            "print('ok')\n")
+    env = dict(os.environ, PYTHONPATH=os.pathsep.join([b200ar.shim.shim_path(), root]))
+    res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0 and res.stdout.strip().endswith("ok"), res.stderr[-2000:]
