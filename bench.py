@@ -229,12 +229,49 @@ def capture_graphs(fn_by_size, sz_list):
     return graphs
 
 
+def summarize(per_call, sz_list, world, variant_of, graphs_on, nccl_on, nccl_graphs_on):
+    """Per-size rows, the headline value and the crossover fields from
+    per-call latencies in us (each already the max over ranks), keyed
+    ``<mode>/<bytes>`` with modes eager, graph, nccl_eager and nccl_graph."""
+    from b200ar.parallel.selector import crossover_bytes, parity_band
+    from b200ar.utils.timing import allreduce_bandwidth, geomean, latency_stats, percentile
+
+    p50 = {key: percentile(v, 50) for key, v in per_call.items()}
+    stats = {key: latency_stats(v) for key, v in per_call.items()}
+    sweep = []
+    cross_rows = {"eager": [], "graph": []}
+    for s in sz_list:
+        row = {"bytes": s, "variant": variant_of(s), "eager_p50_us": round(p50[f"eager/{s}"], 3)}
+        if graphs_on:
+            row["graph_p50_us"] = round(p50[f"graph/{s}"], 3)
+        if nccl_on:
+            row["nccl_eager_p50_us"] = round(p50[f"nccl_eager/{s}"], 3)
+            if nccl_graphs_on:
+                row["nccl_graph_p50_us"] = round(p50[f"nccl_graph/{s}"], 3)
+        row["eager_us"] = stats[f"eager/{s}"]
+        if graphs_on:
+            row["graph_us"] = stats[f"graph/{s}"]
+        if world > 1:
+            row.update(allreduce_bandwidth(s, world, p50[f"eager/{s}"]))
+        sweep.append(row)
+        for mode in ("eager", "graph"):
+            if f"{mode}/{s}" in p50 and f"nccl_{mode}/{s}" in p50:
+                cross_rows[mode] += [
+                    {"bytes": s, "impl": "custom", "us": p50[f"{mode}/{s}"]},
+                    {"bytes": s, "impl": "nccl", "us": p50[f"nccl_{mode}/{s}"]},
+                ]
+    value = round(geomean([r["eager_p50_us"] for r in sweep]), 3)
+    cross = {}
+    if nccl_on:
+        cross["crossover_bytes"] = {m: crossover_bytes(r) for m, r in cross_rows.items() if r}
+        cross["crossover_band_bytes"] = {m: parity_band(r) for m, r in cross_rows.items() if r}
+    return sweep, value, cross
+
+
 def run(args):
     sys.path.insert(0, ROOT)
     from b200ar.utils.clocks import ClockSampler
-    from b200ar.utils.timing import (EventTimer, L2Flusher, allreduce_bandwidth, geomean, latency_stats,
-                                     max_over_ranks, percentile)
-    from b200ar.parallel.selector import crossover_bytes, parity_band
+    from b200ar.utils.timing import EventTimer, L2Flusher, geomean, max_over_ranks, percentile
 
     rank, world, local, gloo = init_dist(args.gpus)
     dev = torch.device("cuda", local)
@@ -301,8 +338,6 @@ def run(args):
     total_ms = max_over_ranks([t0.elapsed_time(t1)], dev)[0]
     times = timer.times_ms()
     per_call = {key: [v * 1e3 for v in max_over_ranks(vals, dev)] for key, vals in times.items()}  # µs
-    p50 = {key: percentile(v, 50) for key, v in per_call.items()}
-    stats = {key: latency_stats(v) for key, v in per_call.items()}
     clocks = sampler.summary() if local == 0 else {}
 
     # ---- end to end through the public API: pinned H2D, all-reduce, D2H ----
@@ -333,32 +368,11 @@ def run(args):
             "per_size_p50_us": {str(s): round(v, 2) for s, v in e2e_p50.items()},
         }
 
-    sweep = []
-    cross_rows = {"eager": [], "graph": []}
-    for s in sz_list:
-        row = {"bytes": s, "variant": arm.variant(s), "eager_p50_us": round(p50[f"eager/{s}"], 3)}
-        if graphs:
-            row["graph_p50_us"] = round(p50[f"graph/{s}"], 3)
-        if with_nccl:
-            row["nccl_eager_p50_us"] = round(p50[f"nccl_eager/{s}"], 3)
-            if nccl_graphs:
-                row["nccl_graph_p50_us"] = round(p50[f"nccl_graph/{s}"], 3)
-        row["eager_us"] = stats[f"eager/{s}"]
-        if graphs:
-            row["graph_us"] = stats[f"graph/{s}"]
-        if world > 1:
-            row.update(allreduce_bandwidth(s, world, p50[f"eager/{s}"]))
-        sweep.append(row)
-        for mode in ("eager", "graph"):
-            if f"{mode}/{s}" in p50 and f"nccl_{mode}/{s}" in p50:
-                cross_rows[mode] += [
-                    {"bytes": s, "impl": "custom", "us": p50[f"{mode}/{s}"]},
-                    {"bytes": s, "impl": "nccl", "us": p50[f"nccl_{mode}/{s}"]},
-                ]
-    value = geomean([r["eager_p50_us"] for r in sweep])
+    sweep, value, cross = summarize(per_call, sz_list, world, arm.variant, bool(graphs), with_nccl,
+                                    bool(nccl_graphs))
     result = {
         "metric": METRIC,
-        "value": round(value, 3),
+        "value": value,
         "unit": "us (geomean over sizes of per-size p50, device time, max over ranks)",
         "n_gpus": world,
         "steps": args.steps,
@@ -383,9 +397,7 @@ def run(args):
         "clocks": clocks,
         "sweep": sweep,
     }
-    if with_nccl:
-        result["crossover_bytes"] = {m: crossover_bytes(r) for m, r in cross_rows.items() if r}
-        result["crossover_band_bytes"] = {m: parity_band(r) for m, r in cross_rows.items() if r}
+    result.update(cross)
     if e2e:
         result["e2e"] = e2e
     arm.close()

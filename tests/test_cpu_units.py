@@ -253,3 +253,39 @@ def test_reference_import_names_resolve_to_b200ar():
     env = dict(os.environ, PYTHONPATH=os.pathsep.join([b200ar.shim.shim_path(), root]))
     res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert res.returncode == 0 and res.stdout.strip().endswith("ok"), res.stderr[-2000:]
+
+
+def _load_bench():
+    import importlib.util
+    import os
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("bench_main", os.path.join(root, "bench.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_bench_summary_rows_and_crossover():
+    bench = _load_bench()
+    sizes = bench.sizes(4096, 4 * 4096)
+    assert sizes == [4096, 8192, 16384]
+    per_call = {}
+    for s in sizes:
+        ours = 10.0 if s < 16384 else 40.0
+        per_call[f"eager/{s}"] = [ours, ours + 1, ours + 2]
+        per_call[f"graph/{s}"] = [ours - 1] * 3
+        per_call[f"nccl_eager/{s}"] = [30.0] * 3
+        per_call[f"nccl_graph/{s}"] = [30.0] * 3
+    sweep, value, cross = bench.summarize(per_call, sizes, 8, lambda s: "lamport", True, True, True)
+    assert [r["bytes"] for r in sweep] == sizes
+    r0 = sweep[0]
+    assert r0["eager_p50_us"] == 11.0 and r0["graph_p50_us"] == 9.0 and r0["nccl_eager_p50_us"] == 30.0
+    assert r0["eager_us"] == {"p10": 10.2, "p50": 11.0, "p90": 11.8, "max": 12.0}
+    assert r0["busbw_gbs"] == round(4096 / 11e-6 / 1e9 * 14 / 8, 1) and "busbw_frac_of_nvlink" in r0
+    assert value == round((11.0 * 11.0 * 41.0) ** (1 / 3), 3)
+    # NCCL is faster only at the largest size: that is the crossover.
+    assert cross["crossover_bytes"] == {"eager": 16384, "graph": 16384}
+    assert cross["crossover_band_bytes"]["eager"] == []
+    sweep1, _, cross1 = bench.summarize({f"eager/{s}": [5.0] for s in sizes}, sizes, 1, str, False, False, False)
+    assert cross1 == {} and "busbw_gbs" not in sweep1[0] and "graph_p50_us" not in sweep1[0]
