@@ -336,6 +336,15 @@ class CustomAllreduce:
                 "message cannot be served by the custom kernels (size/alignment/capacity) and no NCCL group "
                 "was given for the fallback"
             )
+        n = inp.numel()
+        if (out.data_ptr() != inp.data_ptr() and self.world > 1 and n % self.world == 0 and inp.is_contiguous()
+                and out.is_contiguous()):
+            # Out of place without the extra copy: reduce-scatter into this
+            # rank's shard of `out`, then an in-place all-gather of the shards.
+            shard = out.view(-1).narrow(0, self.rank * (n // self.world), n // self.world)
+            dist.reduce_scatter_tensor(shard, inp.view(-1), group=self.nccl_group)
+            dist.all_gather_into_tensor(out.view(-1), shard, group=self.nccl_group)
+            return out
         if out.data_ptr() != inp.data_ptr():
             out.copy_(inp)
         dist.all_reduce(out, group=self.nccl_group)
