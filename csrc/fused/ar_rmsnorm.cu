@@ -273,15 +273,24 @@ __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_lamport_cluster_ker
   const uint4 marker = make_uint4(kLamportMarker, kLamportMarker, kLamportMarker, kLamportMarker);
   for (int64_t row = group; row < a.rows; row += groups) {
     const char* src = mine + row * row_bytes;
-    // Bounded wait for every source's packets of this slice.
+    // Bounded wait for every source's packets of this slice. All packets are
+    // loaded first, so the common case costs one round trip.
+    bool ready[PPT][N];
 #pragma unroll
     for (int k = 0; k < PPT; ++k) {
       const int i = threadIdx.x + k * blockDim.x;
-      if (i >= plen) continue;
+#pragma unroll
+      for (int q = 0; q < N; ++q)
+        ready[k][q] = i >= plen || lamport_ready(ld_volatile16(src + static_cast<int64_t>(q) * a.lam_cap +
+                                                                static_cast<int64_t>(p0 + i) * 16));
+    }
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+      const int i = threadIdx.x + k * blockDim.x;
 #pragma unroll
       for (int q = 0; q < N; ++q) {
+        if (ready[k][q]) continue;
         const char* pk = src + static_cast<int64_t>(q) * a.lam_cap + static_cast<int64_t>(p0 + i) * 16;
-        if (lamport_ready(ld_volatile16(pk))) continue;
         const uint64_t start = global_ns();
         uint32_t spins = 0;
         while (!lamport_ready(ld_volatile16(pk))) {
