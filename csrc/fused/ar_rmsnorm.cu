@@ -16,6 +16,11 @@
 //  * twoshot: rows are split into N parts; rank p reduces and normalises part p,
 //    then every rank pulls the finished y and z rows of the other parts
 //    (2(N-1)/N of the bytes of one-shot's (N-1)).
+//  * lamport: barrier-free one-shot (marker protocol); for decode batches the
+//    cluster form splits every row over the C CTAs of a thread-block cluster
+//    and combines the sum of squares through distributed shared memory.
+#include <cooperative_groups.h>
+
 #include <algorithm>
 #include <stdexcept>
 
@@ -217,6 +222,144 @@ __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_lamport_kernel(Norm
   finish_generation(a.ctx, gen);
 }
 
+// Cluster form of the Lamport kernel for decode batches. The C CTAs of a
+// thread-block cluster share each row: CTA c pushes, polls, reduces and
+// normalises packets [c * S, c * S + S) of the row (S = ceil(hp / C)), so
+// C SMs move the row instead of one. The row's sum of squares is the sum of
+// the C per-CTA partials, read from the other CTAs' shared memory (DSMEM)
+// after a cluster barrier. A bounded poll that expires marks the CTA failed;
+// the flags are combined through DSMEM too, so every CTA of the cluster leaves
+// the row loop at the same point and the cluster barriers stay matched.
+template <int N, int PPT>
+__global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_lamport_cluster_kernel(NormArgs a) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  __shared__ uint32_t s_gen;
+  __shared__ float red[32];
+  __shared__ float s_part;  // this CTA's sum of squares of the current row slice
+  __shared__ int s_fail;
+  const uint32_t gen = read_generation(a.ctx, &s_gen);
+  const int C = static_cast<int>(cluster.num_blocks());
+  const int crank = static_cast<int>(cluster.block_rank());
+  const int group = static_cast<int>(blockIdx.x) / C, groups = static_cast<int>(gridDim.x) / C;
+  const int slice = (a.hp + C - 1) / C;
+  const int p0 = crank * slice;
+  const int plen = max(0, min(slice, a.hp - p0));
+  const int r = a.ctx.rank;
+  const int64_t row_bytes = static_cast<int64_t>(a.hp) * 16;
+  const int64_t buf = static_cast<int64_t>(gen % kLamportBuffers) * N * a.lam_cap;
+  char* dst[N];
+  rotate_ptrs<N>(a.lam, r, dst);
+  for (int64_t row = group; row < a.rows; row += groups) {
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+      const int i = threadIdx.x + k * blockDim.x;
+      if (i < plen) {
+        const int64_t idx = p0 + i;
+        uint4 v = ld_in(a.x + (row * a.hp + idx) * 16);
+        v.x = lamport_clean<__nv_bfloat16>(v.x);
+        v.y = lamport_clean<__nv_bfloat16>(v.y);
+        v.z = lamport_clean<__nv_bfloat16>(v.z);
+        v.w = lamport_clean<__nv_bfloat16>(v.w);
+        const int64_t off = buf + static_cast<int64_t>(r) * a.lam_cap + row * row_bytes + idx * 16;
+#pragma unroll
+        for (int p = 0; p < N; ++p) st_cg(dst[p] + off, v);
+      }
+    }
+  }
+  char* mine = a.lam[r] + buf;
+  if (threadIdx.x == 0) s_fail = 0;
+  __syncthreads();
+  const uint4 marker = make_uint4(kLamportMarker, kLamportMarker, kLamportMarker, kLamportMarker);
+  for (int64_t row = group; row < a.rows; row += groups) {
+    const char* src = mine + row * row_bytes;
+    // Bounded wait for every source's packets of this slice. All packets are
+    // loaded first, so the common case costs one round trip.
+    bool ready[PPT][N];
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+      const int i = threadIdx.x + k * blockDim.x;
+#pragma unroll
+      for (int q = 0; q < N; ++q)
+        ready[k][q] = i >= plen || lamport_ready(ld_volatile16(src + static_cast<int64_t>(q) * a.lam_cap +
+                                                                static_cast<int64_t>(p0 + i) * 16));
+    }
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+      const int i = threadIdx.x + k * blockDim.x;
+#pragma unroll
+      for (int q = 0; q < N; ++q) {
+        if (ready[k][q]) continue;
+        const char* pk = src + static_cast<int64_t>(q) * a.lam_cap + static_cast<int64_t>(p0 + i) * 16;
+        const uint64_t start = global_ns();
+        uint32_t spins = 0;
+        while (!lamport_ready(ld_volatile16(pk))) {
+          if ((++spins & 63u) == 0u && global_ns() - start > a.ctx.timeout_ns) {
+            report_status(a.ctx.status, kStatusTimeout, r, q, blockIdx.x, gen, 0);
+            s_fail = 1;
+            break;
+          }
+        }
+      }
+    }
+    const int failed = __syncthreads_or(s_fail);
+    // Sum the sources, add the residual, keep z (rounded) in registers.
+    float zf[PPT][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+      const int i = threadIdx.x + k * blockDim.x;
+      if (failed || i >= plen) continue;
+      const int64_t idx = p0 + i;
+      uint4 v[N];
+#pragma unroll
+      for (int q = 0; q < N; ++q) v[q] = ld_cg(src + static_cast<int64_t>(q) * a.lam_cap + idx * 16);
+      float acc[8];
+      unpack_set<__nv_bfloat16>(v[0], acc);
+#pragma unroll
+      for (int q = 1; q < N; ++q) unpack_add<__nv_bfloat16>(v[q], acc);
+      unpack_add<__nv_bfloat16>(ld_in(a.res + (row * a.hp + idx) * 16), acc);
+      const uint4 zp = pack<__nv_bfloat16>(acc);
+      st_out(a.z + (row * a.hp + idx) * 16, zp);
+      unpack_set<__nv_bfloat16>(zp, zf[k]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += zf[k][e] * zf[k][e];
+    }
+    const float part = block_sum(ss, red);
+    if (threadIdx.x == 0) {
+      s_part = part;
+      s_fail = failed;
+    }
+    cluster.sync();
+    float tot = 0.f;
+    int any_fail = 0;
+    for (int c = 0; c < C; ++c) {
+      tot += *cluster.map_shared_rank(&s_part, c);
+      any_fail |= *cluster.map_shared_rank(&s_fail, c);
+    }
+    if (any_fail) {
+      cluster.sync();  // peers may still read this CTA's flags
+      break;
+    }
+    const float inv = rsqrtf(tot * a.inv_h + a.eps);
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+      const int i = threadIdx.x + k * blockDim.x;
+      if (i >= plen) continue;
+      const int64_t idx = p0 + i;
+      float g[8];
+      unpack_set<__nv_bfloat16>(ld_in(a.gamma + idx * 16), g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) zf[k][e] = zf[k][e] * inv * g[e];
+      st_out(a.y + (row * a.hp + idx) * 16, pack<__nv_bfloat16>(zf[k]));
+      for (int q = 0; q < N; ++q)
+        st_cg(mine + static_cast<int64_t>(q) * a.lam_cap + row * row_bytes + idx * 16, marker);
+    }
+    cluster.sync();  // s_part and s_fail are rewritten for the next row
+  }
+  finish_generation(a.ctx, gen);
+}
+
 // Two-shot. Part p = rows [part_begin(T, N, p), part_begin(T, N, p + 1)); with
 // prow = ceil(T / N) rows per part, every slot holds
 //   inbox  [N][prow] rows : rank q's partial rows of this rank's part
@@ -316,6 +459,48 @@ void launch_ppt(int world, int kind, int ctas, int threads, const NormArgs& a, c
   }
 }
 
+// Cluster launch of the Lamport kernel: `groups` clusters of C CTAs, a row
+// per cluster at a time.
+template <int N, int PPT>
+void launch_cluster_n(int C, int groups, int threads, const NormArgs& a, cudaStream_t s) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(C * groups));
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(C);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B200AR_CUDA(cudaLaunchKernelEx(&cfg, ar_rmsnorm_lamport_cluster_kernel<N, PPT>, a));
+}
+
+template <int PPT>
+void launch_cluster_ppt(int world, int C, int groups, int threads, const NormArgs& a, cudaStream_t s) {
+  switch (world) {
+    case 2: launch_cluster_n<2, PPT>(C, groups, threads, a, s); break;
+    case 3: launch_cluster_n<3, PPT>(C, groups, threads, a, s); break;
+    case 4: launch_cluster_n<4, PPT>(C, groups, threads, a, s); break;
+    case 5: launch_cluster_n<5, PPT>(C, groups, threads, a, s); break;
+    case 6: launch_cluster_n<6, PPT>(C, groups, threads, a, s); break;
+    case 7: launch_cluster_n<7, PPT>(C, groups, threads, a, s); break;
+    case 8: launch_cluster_n<8, PPT>(C, groups, threads, a, s); break;
+    default: throw std::invalid_argument("the Lamport variant needs 2 to 8 ranks");
+  }
+}
+
+// Rows up to which the Lamport variant runs in cluster form, and the cluster
+// size (portable maximum 8; at least 32 packets per CTA).
+constexpr int64_t kClusterMaxRows = 64;
+int cluster_size(int hp) {
+  int c = 8;
+  while (c > 1 && hp / c < 32) c >>= 1;
+  return c;
+}
+
 }  // namespace
 
 int64_t ar_rmsnorm_slot_bytes(int variant, int64_t rows, int64_t hidden, int world) {
@@ -375,6 +560,20 @@ int ar_rmsnorm(Communicator& comm, cudaStream_t stream, const void* x, const voi
   a.inv_h = 1.0f / static_cast<float>(hidden);
   for (int i = 0; i < world; ++i) a.lam[i] = comm.lamport_ptr(i);
   a.lam_cap = comm.lamport_capacity();
+  if (variant == kLamport && ctas == 0 && rows <= kClusterMaxRows && cluster_size(a.hp) > 1) {
+    const int C = cluster_size(a.hp);
+    const int slice = (a.hp + C - 1) / C;
+    const int cppt = slice <= kMaxRowThreads ? 1 : (slice <= 2 * kMaxRowThreads ? 2 : 4);
+    const int cthreads = std::max(32, ((slice + cppt - 1) / cppt + 31) / 32 * 32);
+    const int groups = static_cast<int>(std::min<int64_t>(rows, kMaxCTAs / C));
+    switch (cppt) {
+      case 1: launch_cluster_ppt<1>(world, C, groups, cthreads, a, stream); break;
+      case 2: launch_cluster_ppt<2>(world, C, groups, cthreads, a, stream); break;
+      default: launch_cluster_ppt<4>(world, C, groups, cthreads, a, stream); break;
+    }
+    comm.count_launch();
+    return variant;
+  }
   const int ppt = a.hp <= kMaxRowThreads ? 1 : (a.hp <= 2 * kMaxRowThreads ? 2 : 4);
   const int threads = std::max(32, ((a.hp + ppt - 1) / ppt + 31) / 32 * 32);
   const bool two = variant == kTwoshot;
