@@ -80,3 +80,28 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
     else:
         _C.gemm_bf16(x2, w, out2, error_word(x.device), max_ctas)
     return out.view(*shp[:-1], n)
+
+
+def linear_silu_gate(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+                     scratch: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``silu(x @ Wg^T) * (x @ Wu^T)`` where the rows of ``w`` [2 I, K] hold the
+    gate and up projections interleaved in groups of 64 (rows 128 j .. 128 j +
+    63 gate, the next 64 the matching up rows). Decode batches (rows <= 128)
+    run one tcgen05 GEMM whose split-K reduction applies the activation; other
+    shapes run the GEMM into ``scratch`` [rows, 2 I] and the activation kernel."""
+    from .layers import silu_mul
+
+    x2 = x.reshape(-1, x.shape[-1])
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    m, n = x2.shape[0], w.shape[0]
+    if out is None:
+        out = torch.empty(m, n // 2, dtype=torch.bfloat16, device=x.device)
+    if x.device.type == "cpu" or m > 128 or n % 128:
+        gu = linear(x2, w, out=scratch)
+        return silu_mul(gu.view(m, n), out=out, group=64)
+    ws = _skinny_workspace(x.device, 1, m, n)
+    splits = _C.skinny_splits(n, x2.shape[1], ws["sms"])
+    ws = _skinny_workspace(x.device, splits, m, n)
+    _C.gemm_skinny(x2, w, out.view(m, n // 2), ws["partials"], ws["counters"], error_word(x.device), splits, 1)
+    return out

@@ -30,9 +30,12 @@ void gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int6
 // Decode GEMM for M <= 128 (swap-AB, split-K over `splits` CTAs per 128-row
 // weight block). `partials` (fp32 [splits, M, N]) and `counters` (zeroed
 // uint32 [ceil(N / 128)]) are needed when splits > 1; calls that share them
-// must be ordered on one stream.
+// must be ordered on one stream. `epilogue` 1 treats W as gate and up rows
+// interleaved in groups of 64 and writes silu(gate) * up to out[M, N / 2]
+// (N a multiple of 128; partials and counters are needed for every split
+// count).
 int skinny_splits(int64_t N, int64_t K, int sms);
 void gemm_skinny(const void* x, const void* w, void* out, float* partials, unsigned* counters, int64_t M, int64_t N,
-                 int64_t K, int splits, int* err, cudaStream_t stream);
+                 int64_t K, int splits, int* err, cudaStream_t stream, int epilogue = 0);
 
 }  // namespace b200ar

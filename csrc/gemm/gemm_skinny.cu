@@ -13,6 +13,12 @@
 // block (per-block arrival counter) sums the partials in split order and
 // writes bf16, so results do not depend on arrival order. The counter is
 // reset by that last CTA for the next call.
+// Epilogue mode 1 (SiLU-gate): the weight rows hold gate and up projections
+// interleaved in groups of 64 (rows [128 b, 128 b + 64) = gate rows
+// [64 b, 64 b + 64), the next 64 rows = the matching up rows). The partials
+// always go through the reduction, which rounds g and u to bf16 (as a stored
+// gate-up product would be) and writes silu(g) * u to out[M, N / 2]: the
+// activation kernel and the gate-up round trip disappear.
 #include <cuda.h>
 
 #include <algorithm>
@@ -47,6 +53,7 @@ struct SkinnyArgs {
   unsigned* counters;   // [N / 128] arrival counters, zero between calls
   int M, N, K;
   int nblocks, splits, kblocks;
+  int epi;              // 0: out[M, N] = x W^T; 1: SiLU-gate over 64-row groups, out[M, N / 2]
 };
 
 template <int MP>
@@ -157,7 +164,7 @@ __global__ void __launch_bounds__(STHREADS, 1)
           const int m = c + i;
           if (m < a.M) {
             const float v = have ? __uint_as_float(r[i]) : 0.f;
-            if (a.splits == 1)
+            if (a.splits == 1 && a.epi == 0)
               a.out[static_cast<int64_t>(m) * a.N + n] = __float2bfloat16_rn(v);
             else
               a.partials[(static_cast<int64_t>(sp) * a.M + m) * a.N + n] = v;
@@ -176,7 +183,7 @@ __global__ void __launch_bounds__(STHREADS, 1)
     if (threadIdx.x == 0) atomicExch(err, 1);
     return;
   }
-  if (a.splits == 1) return;
+  if (a.splits == 1 && a.epi == 0) return;
   // Split-K: the last CTA of this row block sums the partials in split order.
   __threadfence();
   __syncthreads();
@@ -184,7 +191,60 @@ __global__ void __launch_bounds__(STHREADS, 1)
   __syncthreads();
   if (!*s_last) return;
   __threadfence();
-  {
+  if (a.epi == 1) {
+    // thread item = (row m, 4 consecutive gate columns c of this block and the
+    // 4 up columns c + 64); sums in split order, then the activation.
+    constexpr int HALF = SBM / 2;
+    const int64_t sstride = static_cast<int64_t>(a.M) * a.N;
+    const int64_t on = a.N / 2;
+    const int items = a.M * (HALF / 4);
+    for (int i0 = threadIdx.x; i0 < items; i0 += 2 * STHREADS) {
+      float4 g[2], u[2];
+      int64_t off[2], oo[2];
+      bool act[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int it = i0 + j * STHREADS;
+        const int m = it / (HALF / 4), c = (it % (HALF / 4)) * 4;
+        act[j] = it < items && b * SBM + HALF + c < a.N;
+        off[j] = static_cast<int64_t>(m) * a.N + b * SBM + c;
+        oo[j] = static_cast<int64_t>(m) * on + b * HALF + c;
+        g[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        u[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      for (int q = 0; q < a.splits; ++q) {
+        float4 vg[2], vu[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const float* base = a.partials + q * sstride + off[j];
+          vg[j] = act[j] ? __ldcg(reinterpret_cast<const float4*>(base)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          vu[j] = act[j] ? __ldcg(reinterpret_cast<const float4*>(base + HALF)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          g[j].x += vg[j].x; g[j].y += vg[j].y; g[j].z += vg[j].z; g[j].w += vg[j].w;
+          u[j].x += vu[j].x; u[j].y += vu[j].y; u[j].z += vu[j].z; u[j].w += vu[j].w;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        if (act[j]) {
+          const float gs[4] = {g[j].x, g[j].y, g[j].z, g[j].w};
+          const float us[4] = {u[j].x, u[j].y, u[j].z, u[j].w};
+          float y[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float gb = __bfloat162float(__float2bfloat16_rn(gs[e]));
+            const float ub = __bfloat162float(__float2bfloat16_rn(us[e]));
+            y[e] = gb / (1.f + __expf(-gb)) * ub;
+          }
+          uint2 w;
+          w.x = sm100::pack_bf16x2(y[0], y[1]);
+          w.y = sm100::pack_bf16x2(y[2], y[3]);
+          *reinterpret_cast<uint2*>(a.out + oo[j]) = w;
+        }
+    }
+  } else {
     // 16-byte loads: thread item = (row m, 4 consecutive columns of this
     // block); four items and four splits of loads in flight, sums in split order.
     const int64_t sstride = static_cast<int64_t>(a.M) * a.N;
@@ -236,7 +296,7 @@ __global__ void __launch_bounds__(STHREADS, 1)
 
 template <int MP>
 void launch_skinny(const void* x, const void* w, void* out, float* partials, unsigned* counters, int64_t M, int64_t N,
-                   int64_t K, int splits, int* err, cudaStream_t stream) {
+                   int64_t K, int splits, int epi, int* err, cudaStream_t stream) {
   using C = SkinnyCfg<MP>;
   const CUtensorMap tw = make_tmap_bf16_2d(w, N, K, K, SBM, SBK);
   const CUtensorMap tx = make_tmap_bf16_2d(x, M, K, K, MP, SBK);
@@ -250,6 +310,7 @@ void launch_skinny(const void* x, const void* w, void* out, float* partials, uns
   a.nblocks = static_cast<int>((N + SBM - 1) / SBM);
   a.kblocks = static_cast<int>((K + SBK - 1) / SBK);
   a.splits = splits;
+  a.epi = epi;
   auto kern = skinny_kernel<MP>;
   static PerDeviceOnce smem_attr;
   smem_attr([&] {
@@ -270,19 +331,22 @@ int skinny_splits(int64_t N, int64_t K, int sms) {
 }
 
 void gemm_skinny(const void* x, const void* w, void* out, float* partials, unsigned* counters, int64_t M, int64_t N,
-                 int64_t K, int splits, int* err, cudaStream_t stream) {
+                 int64_t K, int splits, int* err, cudaStream_t stream, int epilogue) {
   const TraceRange trace("b200ar::gemm_skinny");
   B200AR_CHECK(M >= 1 && M <= SBM, "skinny GEMM serves 1 <= M <= 128, got " << M);
   B200AR_CHECK(K % 8 == 0 && N % 8 == 0, "K and N must be multiples of 8");
-  B200AR_CHECK(splits >= 1 && (splits == 1 || (partials && counters)), "split-K needs partials and counters");
+  B200AR_CHECK(epilogue == 0 || epilogue == 1, "unknown skinny GEMM epilogue " << epilogue);
+  B200AR_CHECK(epilogue == 0 || N % SBM == 0, "the SiLU-gate epilogue needs N (gate + up rows) a multiple of 128");
+  B200AR_CHECK((splits == 1 && epilogue == 0) || (partials && counters), "split-K needs partials and counters");
+  B200AR_CHECK(splits >= 1, "splits must be positive");
   if (M <= 16)
-    launch_skinny<16>(x, w, out, partials, counters, M, N, K, splits, err, stream);
+    launch_skinny<16>(x, w, out, partials, counters, M, N, K, splits, epilogue, err, stream);
   else if (M <= 32)
-    launch_skinny<32>(x, w, out, partials, counters, M, N, K, splits, err, stream);
+    launch_skinny<32>(x, w, out, partials, counters, M, N, K, splits, epilogue, err, stream);
   else if (M <= 64)
-    launch_skinny<64>(x, w, out, partials, counters, M, N, K, splits, err, stream);
+    launch_skinny<64>(x, w, out, partials, counters, M, N, K, splits, epilogue, err, stream);
   else
-    launch_skinny<128>(x, w, out, partials, counters, M, N, K, splits, err, stream);
+    launch_skinny<128>(x, w, out, partials, counters, M, N, K, splits, epilogue, err, stream);
 }
 
 }  // namespace b200ar

@@ -57,3 +57,28 @@ def test_skinny_gemm_matches_fp32(m, n, k):
         ref = a.float() @ w.float().t()
         err = (out.float() - ref).abs().max().item()
         assert err <= 1e-2 * ref.abs().max().item() + 1e-2, (m, n, k, err)
+
+
+@pytest.mark.parametrize("m,inter,k", [(1, 3584, 8192), (8, 3584, 8192), (64, 512, 1024), (128, 1024, 256),
+                                       (200, 512, 256)])
+def test_linear_silu_gate_fused_epilogue(m, inter, k):
+    """The fused SiLU-gate epilogue equals the GEMM followed by the activation
+    kernel bit for bit (same split order, same bf16 rounding of gate and up),
+    and both match an fp32 reference."""
+    from b200ar.ops.gemm import check_errors, linear, linear_silu_gate
+    from b200ar.ops.layers import ref_silu_mul, silu_mul
+
+    g = torch.Generator(device="cuda").manual_seed(m + inter + k)
+    x = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+    w = (0.02 * torch.randn(2 * inter, k, generator=g, device="cuda")).to(torch.bfloat16)
+    fused = linear_silu_gate(x, w)
+    two_step = silu_mul(linear(x, w), group=64)
+    torch.cuda.synchronize()
+    check_errors()
+    assert torch.equal(fused, two_step)
+    ref = ref_silu_mul((x.float() @ w.float().t()).to(torch.bfloat16), group=64)
+    torch.testing.assert_close(fused.float(), ref.float(), atol=2e-2, rtol=2e-2)
+    for _ in range(3):  # repeated calls re-arm the split-K counters
+        again = linear_silu_gate(x, w)
+    torch.cuda.synchronize()
+    assert torch.equal(again, fused)
