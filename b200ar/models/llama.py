@@ -7,8 +7,7 @@ batch 1 / 8 / 32 / 64 under CUDA graphs, two fused all-reduces per layer.
 
 Per rank (tensor parallel over ``world`` GPUs) one decode step of a layer is
 
-    qkv  = h @ Wqkv^T                         column parallel (tcgen05 GEMM)
-    q,kv = rope(qkv); kv -> cache             rope_kv kernel
+    q,kv = rope(h @ Wqkv^T); kv -> cache      column parallel, RoPE + cache write fused into the GEMM
     a    = attention(q, cache)                GQA decode attention kernel
     o    = a @ Wo^T                           row parallel, partial sums
     h, x = RMSNorm(all_reduce(o) + x)         fused all-reduce + residual + RMSNorm
@@ -33,8 +32,8 @@ from typing import List, Optional
 import torch
 import torch.distributed as dist
 
-from ..ops.gemm import linear, linear_silu_gate
-from ..ops.layers import RotaryTable, decode_attention, rmsnorm, rope_kv, split_gate_up
+from ..ops.gemm import linear, linear_rope_kv, linear_silu_gate
+from ..ops.layers import RotaryTable, decode_attention, rmsnorm, split_gate_up
 
 
 @dataclasses.dataclass
@@ -144,8 +143,8 @@ class TPLlamaDecoder:
         cfg = self.cfg
         if first:
             rmsnorm(self.x, L["g_attn"], cfg.eps, out=self.h)
-        linear(self.h, L["wqkv"], out=self.qkv)
-        rope_kv(self.qkv, self.pos, self.rot, self.q, self.k_cache[i], self.v_cache[i], self.hq, self.hkv)
+        linear_rope_kv(self.h, L["wqkv"], self.pos, self.rot, self.q, self.k_cache[i], self.v_cache[i], self.hq,
+                       self.hkv, scratch=self.qkv)
         decode_attention(self.q, self.k_cache[i], self.v_cache[i], self.seq_len, self.hq, self.hkv, out=self.attn)
         linear(self.attn, L["wo"], out=self.part)
         self.comm.all_reduce_residual_rmsnorm(self.part, self.x, L["g_mlp"], cfg.eps, out=self.h,

@@ -105,3 +105,27 @@ def linear_silu_gate(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tenso
     ws = _skinny_workspace(x.device, splits, m, n)
     _C.gemm_skinny(x2, w, out.view(m, n // 2), ws["partials"], ws["counters"], error_word(x.device), splits, 1)
     return out
+
+
+def linear_rope_kv(x: torch.Tensor, wqkv: torch.Tensor, pos: torch.Tensor, rot, q_out: torch.Tensor,
+                   k_cache: torch.Tensor, v_cache: torch.Tensor, hq: int, hkv: int,
+                   scratch: Optional[torch.Tensor] = None) -> None:
+    """QKV projection with RoPE and the KV-cache write: ``qkv = x @ Wqkv^T``
+    (heads of 128 rows, [q | k | v]); q and k rotated at ``pos`` (rotate-half),
+    q to ``q_out`` [B, hq, 128], k and v into the caches [B, L, hkv, 128] at
+    ``pos``. Decode batches (rows <= 128, head_dim 128) run one tcgen05 GEMM
+    whose split-K reduction does the rotation and the cache write; other
+    shapes run the GEMM into ``scratch`` and the RoPE kernel."""
+    from .layers import rope_kv
+
+    m, n = x.shape[0], wqkv.shape[0]
+    if x.device.type == "cpu" or m > 128 or rot.head_dim != 128 or n != (hq + 2 * hkv) * 128:
+        qkv = linear(x, wqkv, out=scratch)
+        rope_kv(qkv, pos, rot, q_out, k_cache, v_cache, hq, hkv)
+        return
+    x2 = x if x.is_contiguous() else x.contiguous()
+    ws = _skinny_workspace(x.device, 1, m, n)
+    splits = _C.skinny_splits(n, x2.shape[1], ws["sms"])
+    ws = _skinny_workspace(x.device, splits, m, n)
+    _C.gemm_skinny_rope_kv(x2, wqkv, pos, rot.cos, rot.sin, q_out, k_cache, v_cache, ws["partials"],
+                           ws["counters"], error_word(x.device), splits, hq, hkv)
