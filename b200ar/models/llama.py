@@ -7,16 +7,18 @@ batch 1 / 8 / 32 / 64 under CUDA graphs, two fused all-reduces per layer.
 
 Per rank (tensor parallel over ``world`` GPUs) one decode step of a layer is
 
-    qkv  = h @ Wqkv^T                         column parallel (tcgen05 GEMM)
-    q,kv = rope(qkv); kv -> cache             rope_kv kernel
+    q,kv = rope(h @ Wqkv^T); kv -> cache      column parallel, RoPE + cache write fused into the GEMM
     a    = attention(q, cache)                GQA decode attention kernel
     o    = a @ Wo^T                           row parallel, partial sums
     h, x = RMSNorm(all_reduce(o) + x)         fused all-reduce + residual + RMSNorm
-    gu   = h @ Wgu^T ; m = silu(g) * u        column parallel + SiLU-gate kernel
+    m    = silu(h @ Wg^T) * (h @ Wu^T)        column parallel, activation fused into the GEMM
     d    = m @ Wd^T                           row parallel, partial sums
     h, x = RMSNorm(all_reduce(d) + x)         fused, with the next layer's norm weights
 
 The residual stream ``x`` is replicated on every rank, as in Megatron-style TP.
+``Wgu`` stores the gate and up rows interleaved in groups of 64, so each
+128-row block of the decode GEMM holds matching gate and up rows and its
+epilogue can apply the activation.
 ``ReferenceDecoder`` computes the same step with plain PyTorch ops (cuBLAS,
 NCCL all-reduce, PyTorch attention) as the comparison baseline.
 """
@@ -30,8 +32,8 @@ from typing import List, Optional
 import torch
 import torch.distributed as dist
 
-from ..ops.gemm import linear
-from ..ops.layers import RotaryTable, decode_attention, rmsnorm, rope_kv, silu_mul
+from ..ops.gemm import linear, linear_rope_kv, linear_silu_gate
+from ..ops.layers import RotaryTable, decode_attention, rmsnorm, split_gate_up
 
 
 @dataclasses.dataclass
@@ -72,6 +74,8 @@ class TPLlamaDecoder:
         w = self.world
         if cfg.heads % w or cfg.intermediate % w:
             raise ValueError("heads and intermediate size must divide the TP world size")
+        if (cfg.intermediate // w) % 64:
+            raise ValueError("the per-rank intermediate size must be a multiple of 64 (gate/up interleave groups)")
         self.hq = cfg.heads // w
         self.hkv = max(1, cfg.kv_heads // w)
         self.inter = cfg.intermediate // w
@@ -139,14 +143,13 @@ class TPLlamaDecoder:
         cfg = self.cfg
         if first:
             rmsnorm(self.x, L["g_attn"], cfg.eps, out=self.h)
-        linear(self.h, L["wqkv"], out=self.qkv)
-        rope_kv(self.qkv, self.pos, self.rot, self.q, self.k_cache[i], self.v_cache[i], self.hq, self.hkv)
+        linear_rope_kv(self.h, L["wqkv"], self.pos, self.rot, self.q, self.k_cache[i], self.v_cache[i], self.hq,
+                       self.hkv, scratch=self.qkv)
         decode_attention(self.q, self.k_cache[i], self.v_cache[i], self.seq_len, self.hq, self.hkv, out=self.attn)
         linear(self.attn, L["wo"], out=self.part)
         self.comm.all_reduce_residual_rmsnorm(self.part, self.x, L["g_mlp"], cfg.eps, out=self.h,
                                               residual_out=self.x)
-        linear(self.h, L["wgu"], out=self.gu)
-        silu_mul(self.gu, out=self.act)
+        linear_silu_gate(self.h, L["wgu"], out=self.act, scratch=self.gu)
         linear(self.act, L["wd"], out=self.part)
         nxt = self.layers[i + 1]["g_attn"] if i + 1 < len(self.layers) else self.g_final
         self.comm.all_reduce_residual_rmsnorm(self.part, self.x, nxt, cfg.eps, out=self.h, residual_out=self.x)
@@ -241,7 +244,7 @@ class ReferenceDecoder:
             m.x.copy_((part.float() + m.x.float()).to(torch.bfloat16))
             m.h.copy_(self._norm(m.x, L["g_mlp"], cfg.eps))
             gu = m.h @ L["wgu"].t()
-            g, u = gu.chunk(2, dim=-1)
+            g, u = split_gate_up(gu, 64)
             act = (torch.nn.functional.silu(g.float()) * u.float()).to(torch.bfloat16)
             part = act @ L["wd"].t()
             self._ar(part)

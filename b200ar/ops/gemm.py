@@ -80,3 +80,52 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
     else:
         _C.gemm_bf16(x2, w, out2, error_word(x.device), max_ctas)
     return out.view(*shp[:-1], n)
+
+
+def linear_silu_gate(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+                     scratch: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``silu(x @ Wg^T) * (x @ Wu^T)`` where the rows of ``w`` [2 I, K] hold the
+    gate and up projections interleaved in groups of 64 (rows 128 j .. 128 j +
+    63 gate, the next 64 the matching up rows). Decode batches (rows <= 128)
+    run one tcgen05 GEMM whose split-K reduction applies the activation; other
+    shapes run the GEMM into ``scratch`` [rows, 2 I] and the activation kernel."""
+    from .layers import silu_mul
+
+    x2 = x.reshape(-1, x.shape[-1])
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    m, n = x2.shape[0], w.shape[0]
+    if out is None:
+        out = torch.empty(m, n // 2, dtype=torch.bfloat16, device=x.device)
+    if x.device.type == "cpu" or m > 128 or n % 128:
+        gu = linear(x2, w, out=scratch)
+        return silu_mul(gu.view(m, n), out=out, group=64)
+    ws = _skinny_workspace(x.device, 1, m, n)
+    splits = _C.skinny_splits(n, x2.shape[1], ws["sms"])
+    ws = _skinny_workspace(x.device, splits, m, n)
+    _C.gemm_skinny(x2, w, out.view(m, n // 2), ws["partials"], ws["counters"], error_word(x.device), splits, 1)
+    return out
+
+
+def linear_rope_kv(x: torch.Tensor, wqkv: torch.Tensor, pos: torch.Tensor, rot, q_out: torch.Tensor,
+                   k_cache: torch.Tensor, v_cache: torch.Tensor, hq: int, hkv: int,
+                   scratch: Optional[torch.Tensor] = None) -> None:
+    """QKV projection with RoPE and the KV-cache write: ``qkv = x @ Wqkv^T``
+    (heads of 128 rows, [q | k | v]); q and k rotated at ``pos`` (rotate-half),
+    q to ``q_out`` [B, hq, 128], k and v into the caches [B, L, hkv, 128] at
+    ``pos``. Decode batches (rows <= 128, head_dim 128) run one tcgen05 GEMM
+    whose split-K reduction does the rotation and the cache write; other
+    shapes run the GEMM into ``scratch`` and the RoPE kernel."""
+    from .layers import rope_kv
+
+    m, n = x.shape[0], wqkv.shape[0]
+    if x.device.type == "cpu" or m > 128 or rot.head_dim != 128 or n != (hq + 2 * hkv) * 128:
+        qkv = linear(x, wqkv, out=scratch)
+        rope_kv(qkv, pos, rot, q_out, k_cache, v_cache, hq, hkv)
+        return
+    x2 = x if x.is_contiguous() else x.contiguous()
+    ws = _skinny_workspace(x.device, 1, m, n)
+    splits = _C.skinny_splits(n, x2.shape[1], ws["sms"])
+    ws = _skinny_workspace(x.device, splits, m, n)
+    _C.gemm_skinny_rope_kv(x2, wqkv, pos, rot.cos, rot.sin, q_out, k_cache, v_cache, ws["partials"],
+                           ws["counters"], error_word(x.device), splits, hq, hkv)

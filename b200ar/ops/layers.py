@@ -113,20 +113,32 @@ def ref_decode_attention(q, k_cache, v_cache, seq_len, hq: int, hkv: int):
     return out.reshape(b, hq * 128)
 
 
-def silu_mul(gate_up, out=None):
+def silu_mul(gate_up, out=None, group: int = 0):
+    """silu(gate) * up. ``group`` 0: ``gate_up`` is [gate | up]; ``group`` g:
+    gate and up columns alternate in groups of g (the layout whose gate-up
+    GEMM can fuse the activation, see ``b200ar.ops.gemm.linear_silu_gate``)."""
     rows, two_i = gate_up.shape
     if out is None:
         out = torch.empty(rows, two_i // 2, dtype=gate_up.dtype, device=gate_up.device)
     if gate_up.device.type == "cpu":
-        out.copy_(ref_silu_mul(gate_up))
+        out.copy_(ref_silu_mul(gate_up, group))
         return out
     if torch.compiler.is_compiling():
-        torch.ops.b200ar.silu_mul(gate_up, out)
+        torch.ops.b200ar.silu_mul(gate_up, out, group)
         return out
-    _C.silu_mul(gate_up, out)
+    _C.silu_mul(gate_up, out, group)
     return out
 
 
-def ref_silu_mul(gate_up):
-    g, u = gate_up.float().chunk(2, dim=-1)
+def split_gate_up(gate_up, group: int = 0):
+    """(gate, up) views of a gate-up product in either layout of ``silu_mul``."""
+    rows, two_i = gate_up.shape
+    if group == 0:
+        return gate_up.chunk(2, dim=-1)
+    g = gate_up.view(rows, two_i // (2 * group), 2, group)
+    return g[:, :, 0].reshape(rows, -1), g[:, :, 1].reshape(rows, -1)
+
+
+def ref_silu_mul(gate_up, group: int = 0):
+    g, u = split_gate_up(gate_up.float(), group)
     return (torch.nn.functional.silu(g) * u).to(gate_up.dtype)

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -30,9 +31,26 @@ void gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int6
 // Decode GEMM for M <= 128 (swap-AB, split-K over `splits` CTAs per 128-row
 // weight block). `partials` (fp32 [splits, M, N]) and `counters` (zeroed
 // uint32 [ceil(N / 128)]) are needed when splits > 1; calls that share them
-// must be ordered on one stream.
+// must be ordered on one stream. `epilogue` 1 treats W as gate and up rows
+// interleaved in groups of 64 and writes silu(gate) * up to out[M, N / 2]
+// (N a multiple of 128; partials and counters are needed for every split
+// count).
+// `epilogue` 2 treats W as the QKV projection (one 128-row block per head,
+// [q | k | v]) and, instead of writing `out`, rotates q and k (rotate-half
+// RoPE at pos[m]) and writes q to q_out[M, hq, 128] and k, v into the caches
+// [M, max_len, hkv, 128] at pos[m].
+struct RopeKvArgs {
+  const int* pos;
+  const float* cos_t;  // [positions, 64]
+  const float* sin_t;
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  int hq, hkv, max_len;
+};
 int skinny_splits(int64_t N, int64_t K, int sms);
 void gemm_skinny(const void* x, const void* w, void* out, float* partials, unsigned* counters, int64_t M, int64_t N,
-                 int64_t K, int splits, int* err, cudaStream_t stream);
+                 int64_t K, int splits, int* err, cudaStream_t stream, int epilogue = 0,
+                 const RopeKvArgs* rope = nullptr);
 
 }  // namespace b200ar

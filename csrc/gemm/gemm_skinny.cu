@@ -13,6 +13,18 @@
 // block (per-block arrival counter) sums the partials in split order and
 // writes bf16, so results do not depend on arrival order. The counter is
 // reset by that last CTA for the next call.
+// Epilogue mode 1 (SiLU-gate): the weight rows hold gate and up projections
+// interleaved in groups of 64 (rows [128 b, 128 b + 64) = gate rows
+// [64 b, 64 b + 64), the next 64 rows = the matching up rows). The partials
+// always go through the reduction, which rounds g and u to bf16 (as a stored
+// gate-up product would be) and writes silu(g) * u to out[M, N / 2]: the
+// activation kernel and the gate-up round trip disappear.
+// Epilogue mode 2 (RoPE + KV write): W is the QKV projection, one 128-row
+// block per head ([q heads | k heads | v heads], head_dim 128). The reduction
+// rounds each pair (c, c + 64) of a head to bf16, rotates q and k heads by
+// the position of the row's sequence (rotate-half), and writes q heads to
+// q_out[M, hq, 128] and k, v heads into the caches at that position: the
+// separate RoPE kernel and the qkv round trip disappear.
 #include <cuda.h>
 
 #include <algorithm>
@@ -47,6 +59,8 @@ struct SkinnyArgs {
   unsigned* counters;   // [N / 128] arrival counters, zero between calls
   int M, N, K;
   int nblocks, splits, kblocks;
+  int epi;              // 0: out[M, N] = x W^T; 1: SiLU-gate over 64-row groups, out[M, N / 2]; 2: RoPE + KV
+  RopeKvArgs rope;      // epi 2 only
 };
 
 template <int MP>
@@ -157,7 +171,7 @@ __global__ void __launch_bounds__(STHREADS, 1)
           const int m = c + i;
           if (m < a.M) {
             const float v = have ? __uint_as_float(r[i]) : 0.f;
-            if (a.splits == 1)
+            if (a.splits == 1 && a.epi == 0)
               a.out[static_cast<int64_t>(m) * a.N + n] = __float2bfloat16_rn(v);
             else
               a.partials[(static_cast<int64_t>(sp) * a.M + m) * a.N + n] = v;
@@ -176,7 +190,7 @@ __global__ void __launch_bounds__(STHREADS, 1)
     if (threadIdx.x == 0) atomicExch(err, 1);
     return;
   }
-  if (a.splits == 1) return;
+  if (a.splits == 1 && a.epi == 0) return;
   // Split-K: the last CTA of this row block sums the partials in split order.
   __threadfence();
   __syncthreads();
@@ -184,7 +198,102 @@ __global__ void __launch_bounds__(STHREADS, 1)
   __syncthreads();
   if (!*s_last) return;
   __threadfence();
-  {
+  if (a.epi != 0) {
+    // Paired epilogues: thread item = (row m, columns c .. c + 3 of this block
+    // and the partner columns c + 64 .. c + 67); sums in split order, rounded
+    // to bf16 as a stored product would be, then the epilogue.
+    constexpr int HALF = SBM / 2;
+    const int64_t sstride = static_cast<int64_t>(a.M) * a.N;
+    const int items = a.M * (HALF / 4);
+    for (int i0 = threadIdx.x; i0 < items; i0 += 2 * STHREADS) {
+      float4 lo[2], hi[2];
+      int64_t off[2];
+      int mm[2], cc[2];
+      bool act[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int it = i0 + j * STHREADS;
+        mm[j] = it / (HALF / 4);
+        cc[j] = (it % (HALF / 4)) * 4;
+        act[j] = it < items && b * SBM + HALF + cc[j] < a.N;
+        off[j] = static_cast<int64_t>(mm[j]) * a.N + b * SBM + cc[j];
+        lo[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        hi[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      for (int q = 0; q < a.splits; ++q) {
+        float4 vl[2], vh[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const float* base = a.partials + q * sstride + off[j];
+          vl[j] = act[j] ? __ldcg(reinterpret_cast<const float4*>(base)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          vh[j] = act[j] ? __ldcg(reinterpret_cast<const float4*>(base + HALF)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          lo[j].x += vl[j].x; lo[j].y += vl[j].y; lo[j].z += vl[j].z; lo[j].w += vl[j].w;
+          hi[j].x += vh[j].x; hi[j].y += vh[j].y; hi[j].z += vh[j].z; hi[j].w += vh[j].w;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        if (!act[j]) continue;
+        const float ls[4] = {lo[j].x, lo[j].y, lo[j].z, lo[j].w};
+        const float hs[4] = {hi[j].x, hi[j].y, hi[j].z, hi[j].w};
+        float x0[4], x1[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          x0[e] = __bfloat162float(__float2bfloat16_rn(ls[e]));
+          x1[e] = __bfloat162float(__float2bfloat16_rn(hs[e]));
+        }
+        const int m = mm[j], c = cc[j];
+        if (a.epi == 1) {
+          // SiLU-gate: x0 = gate, x1 = up; out[m, 64 b + c ..].
+          float y[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) y[e] = x0[e] / (1.f + __expf(-x0[e])) * x1[e];
+          uint2 w;
+          w.x = sm100::pack_bf16x2(y[0], y[1]);
+          w.y = sm100::pack_bf16x2(y[2], y[3]);
+          *reinterpret_cast<uint2*>(a.out + static_cast<int64_t>(m) * (a.N / 2) + b * HALF + c) = w;
+        } else {
+          // RoPE + KV write: block b is head b of [q heads | k heads | v heads].
+          const RopeKvArgs& r = a.rope;
+          const int p = r.pos[m];
+          uint2 w0, w1;
+          if (b < r.hq + r.hkv) {
+            float y0[4], y1[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float cs = r.cos_t[static_cast<int64_t>(p) * HALF + c + e];
+              const float sn = r.sin_t[static_cast<int64_t>(p) * HALF + c + e];
+              y0[e] = x0[e] * cs - x1[e] * sn;
+              y1[e] = x1[e] * cs + x0[e] * sn;
+            }
+            w0.x = sm100::pack_bf16x2(y0[0], y0[1]);
+            w0.y = sm100::pack_bf16x2(y0[2], y0[3]);
+            w1.x = sm100::pack_bf16x2(y1[0], y1[1]);
+            w1.y = sm100::pack_bf16x2(y1[2], y1[3]);
+          } else {
+            w0.x = sm100::pack_bf16x2(x0[0], x0[1]);
+            w0.y = sm100::pack_bf16x2(x0[2], x0[3]);
+            w1.x = sm100::pack_bf16x2(x1[0], x1[1]);
+            w1.y = sm100::pack_bf16x2(x1[2], x1[3]);
+          }
+          __nv_bfloat16* dst;
+          if (b < r.hq) {
+            dst = r.q_out + (static_cast<int64_t>(m) * r.hq + b) * SBM;
+          } else {
+            const bool is_k = b < r.hq + r.hkv;
+            const int kh = is_k ? b - r.hq : b - r.hq - r.hkv;
+            dst = (is_k ? r.k_cache : r.v_cache) +
+                  ((static_cast<int64_t>(m) * r.max_len + p) * r.hkv + kh) * SBM;
+          }
+          *reinterpret_cast<uint2*>(dst + c) = w0;
+          *reinterpret_cast<uint2*>(dst + HALF + c) = w1;
+        }
+      }
+    }
+  } else {
     // 16-byte loads: thread item = (row m, 4 consecutive columns of this
     // block); four items and four splits of loads in flight, sums in split order.
     const int64_t sstride = static_cast<int64_t>(a.M) * a.N;
@@ -236,7 +345,7 @@ __global__ void __launch_bounds__(STHREADS, 1)
 
 template <int MP>
 void launch_skinny(const void* x, const void* w, void* out, float* partials, unsigned* counters, int64_t M, int64_t N,
-                   int64_t K, int splits, int* err, cudaStream_t stream) {
+                   int64_t K, int splits, int epi, const RopeKvArgs* rope, int* err, cudaStream_t stream) {
   using C = SkinnyCfg<MP>;
   const CUtensorMap tw = make_tmap_bf16_2d(w, N, K, K, SBM, SBK);
   const CUtensorMap tx = make_tmap_bf16_2d(x, M, K, K, MP, SBK);
@@ -250,6 +359,8 @@ void launch_skinny(const void* x, const void* w, void* out, float* partials, uns
   a.nblocks = static_cast<int>((N + SBM - 1) / SBM);
   a.kblocks = static_cast<int>((K + SBK - 1) / SBK);
   a.splits = splits;
+  a.epi = epi;
+  if (rope) a.rope = *rope;
   auto kern = skinny_kernel<MP>;
   static PerDeviceOnce smem_attr;
   smem_attr([&] {
@@ -270,19 +381,24 @@ int skinny_splits(int64_t N, int64_t K, int sms) {
 }
 
 void gemm_skinny(const void* x, const void* w, void* out, float* partials, unsigned* counters, int64_t M, int64_t N,
-                 int64_t K, int splits, int* err, cudaStream_t stream) {
+                 int64_t K, int splits, int* err, cudaStream_t stream, int epilogue, const RopeKvArgs* rope) {
   const TraceRange trace("b200ar::gemm_skinny");
   B200AR_CHECK(M >= 1 && M <= SBM, "skinny GEMM serves 1 <= M <= 128, got " << M);
   B200AR_CHECK(K % 8 == 0 && N % 8 == 0, "K and N must be multiples of 8");
-  B200AR_CHECK(splits >= 1 && (splits == 1 || (partials && counters)), "split-K needs partials and counters");
+  B200AR_CHECK(epilogue >= 0 && epilogue <= 2, "unknown skinny GEMM epilogue " << epilogue);
+  B200AR_CHECK(epilogue != 1 || N % SBM == 0, "the SiLU-gate epilogue needs N (gate + up rows) a multiple of 128");
+  B200AR_CHECK(epilogue != 2 || (rope && N == static_cast<int64_t>(rope->hq + 2 * rope->hkv) * SBM),
+               "the RoPE + KV epilogue needs its arguments and N = (hq + 2 hkv) * 128");
+  B200AR_CHECK((splits == 1 && epilogue == 0) || (partials && counters), "split-K needs partials and counters");
+  B200AR_CHECK(splits >= 1, "splits must be positive");
   if (M <= 16)
-    launch_skinny<16>(x, w, out, partials, counters, M, N, K, splits, err, stream);
+    launch_skinny<16>(x, w, out, partials, counters, M, N, K, splits, epilogue, rope, err, stream);
   else if (M <= 32)
-    launch_skinny<32>(x, w, out, partials, counters, M, N, K, splits, err, stream);
+    launch_skinny<32>(x, w, out, partials, counters, M, N, K, splits, epilogue, rope, err, stream);
   else if (M <= 64)
-    launch_skinny<64>(x, w, out, partials, counters, M, N, K, splits, err, stream);
+    launch_skinny<64>(x, w, out, partials, counters, M, N, K, splits, epilogue, rope, err, stream);
   else
-    launch_skinny<128>(x, w, out, partials, counters, M, N, K, splits, err, stream);
+    launch_skinny<128>(x, w, out, partials, counters, M, N, K, splits, epilogue, rope, err, stream);
 }
 
 }  // namespace b200ar

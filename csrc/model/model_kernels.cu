@@ -360,15 +360,22 @@ __global__ void __launch_bounds__(kAttnThreads)
 
 // ------------------------------------------------------------------ SiLU gate
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ y, int inter,
-                                int64_t rows) {
+                                int64_t rows, int group) {
   const int ip = inter / 8;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < rows * ip;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = i / ip, c = i % ip;
     const char* row = reinterpret_cast<const char*>(gu + r * 2 * inter);
+    // Element offsets of this packet's gate and up values.
+    int64_t go = c * 8, uo = static_cast<int64_t>(inter) + c * 8;
+    if (group > 0) {
+      const int64_t j = c * 8;
+      go = (j / group) * 2 * group + j % group;
+      uo = go + group;
+    }
     float g[8], u[8];
-    unpack_set<__nv_bfloat16>(ld_in(row + c * 16), g);
-    unpack_set<__nv_bfloat16>(ld_in(row + static_cast<int64_t>(inter) * 2 + c * 16), u);
+    unpack_set<__nv_bfloat16>(ld_in(row + go * 2), g);
+    unpack_set<__nv_bfloat16>(ld_in(row + uo * 2), u);
 #pragma unroll
     for (int e = 0; e < 8; ++e) g[e] = g[e] / (1.f + __expf(-g[e])) * u[e];
     st_out(reinterpret_cast<char*>(y + r * inter) + c * 16, pack<__nv_bfloat16>(g));
@@ -430,13 +437,16 @@ void decode_attention(const void* q, const void* k_cache, const void* v_cache, c
   B200AR_CUDA(cudaGetLastError());
 }
 
-void silu_mul(const void* gate_up, void* y, int64_t rows, int64_t inter, cudaStream_t s) {
+void silu_mul(const void* gate_up, void* y, int64_t rows, int64_t inter, cudaStream_t s, int group) {
   const TraceRange trace("b200ar::silu_mul");
   B200AR_CHECK(inter % 8 == 0, "intermediate size must be a multiple of 8");
+  B200AR_CHECK(group == 0 || (group % 8 == 0 && inter % group == 0),
+               "interleave group must be a multiple of 8 that divides the intermediate size");
   const int64_t items = rows * inter / 8;
   const int blocks = static_cast<int>(std::min<int64_t>((items + 255) / 256, 4 * 148));
   silu_mul_kernel<<<std::max(blocks, 1), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(gate_up),
-                                                     static_cast<__nv_bfloat16*>(y), static_cast<int>(inter), rows);
+                                                     static_cast<__nv_bfloat16*>(y), static_cast<int>(inter), rows,
+                                                     group);
   B200AR_CUDA(cudaGetLastError());
 }
 

@@ -74,21 +74,27 @@ void register_ops(py::module& m) {
       });
   m.def(
       "silu_mul",
-      [stream](const at::Tensor& gu, at::Tensor& y) {
+      [stream](const at::Tensor& gu, at::Tensor& y, int group) {
+        TORCH_CHECK(gu.is_cuda() && gu.dim() == 2 && gu.is_contiguous() && y.is_contiguous() &&
+                        gu.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16,
+                    "silu_mul takes contiguous bf16 CUDA tensors");
+        TORCH_CHECK(gu.size(1) == 2 * y.size(1) && gu.size(0) == y.size(0), "shape mismatch");
         const at::cuda::OptionalCUDAGuard guard(device_of(gu));
-        b200ar::silu_mul(gu.data_ptr(), y.data_ptr(), gu.size(0), y.size(1), stream());
-      });
+        b200ar::silu_mul(gu.data_ptr(), y.data_ptr(), gu.size(0), y.size(1), stream(), group);
+      },
+      py::arg("gate_up"), py::arg("y"), py::arg("group") = 0);
   m.def("skinny_splits", &b200ar::skinny_splits, py::arg("n"), py::arg("k"), py::arg("sms"));
   m.def(
       "gemm_skinny",
       [](const at::Tensor& x, const at::Tensor& w, at::Tensor& out, at::Tensor& partials, at::Tensor& counters,
-         at::Tensor& err, int splits) {
+         at::Tensor& err, int splits, int epilogue) {
         check_bf16_2d(x, "x");
         check_bf16_2d(w, "W");
         check_bf16_2d(out, "out");
-        TORCH_CHECK(x.size(1) == w.size(1) && out.size(0) == x.size(0) && out.size(1) == w.size(0), "shape mismatch");
+        const int64_t out_cols = epilogue == 1 ? w.size(0) / 2 : w.size(0);
+        TORCH_CHECK(x.size(1) == w.size(1) && out.size(0) == x.size(0) && out.size(1) == out_cols, "shape mismatch");
         TORCH_CHECK(partials.is_cuda() && partials.scalar_type() == at::kFloat &&
-                        partials.numel() >= (splits > 1 ? splits * x.size(0) * w.size(0) : 0),
+                        partials.numel() >= (splits > 1 || epilogue ? splits * x.size(0) * w.size(0) : 0),
                     "partials must be a CUDA float32 tensor of splits * M * N elements");
         TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt &&
                         counters.numel() >= (w.size(0) + 127) / 128,
@@ -96,8 +102,51 @@ void register_ops(py::module& m) {
         const at::cuda::OptionalCUDAGuard guard(device_of(x));
         b200ar::gemm_skinny(x.data_ptr(), w.data_ptr(), out.data_ptr(), partials.data_ptr<float>(),
                             reinterpret_cast<unsigned*>(counters.data_ptr<int>()), x.size(0), w.size(0), x.size(1),
-                            splits, err.data_ptr<int>(), at::cuda::getCurrentCUDAStream().stream());
+                            splits, err.data_ptr<int>(), at::cuda::getCurrentCUDAStream().stream(), epilogue);
       },
-      "decode GEMM (M <= 128): out = x @ W^T, swap-AB tcgen05 with split-K", py::arg("x"), py::arg("w"),
-      py::arg("out"), py::arg("partials"), py::arg("counters"), py::arg("err"), py::arg("splits"));
+      "decode GEMM (M <= 128): out = x @ W^T, swap-AB tcgen05 with split-K; epilogue 1 = SiLU-gate over "
+      "64-row gate/up groups",
+      py::arg("x"), py::arg("w"), py::arg("out"), py::arg("partials"), py::arg("counters"), py::arg("err"),
+      py::arg("splits"), py::arg("epilogue") = 0);
+  m.def(
+      "gemm_skinny_rope_kv",
+      [](const at::Tensor& x, const at::Tensor& w, const at::Tensor& pos, const at::Tensor& cos_t,
+         const at::Tensor& sin_t, at::Tensor& q_out, at::Tensor& k_cache, at::Tensor& v_cache, at::Tensor& partials,
+         at::Tensor& counters, at::Tensor& err, int splits, int hq, int hkv) {
+        check_bf16_2d(x, "x");
+        check_bf16_2d(w, "W");
+        TORCH_CHECK(x.size(1) == w.size(1) && w.size(0) == static_cast<int64_t>(hq + 2 * hkv) * 128,
+                    "W must hold (hq + 2 hkv) heads of 128 rows");
+        TORCH_CHECK(pos.is_cuda() && pos.scalar_type() == at::kInt && pos.numel() >= x.size(0), "pos: int32 [M]");
+        TORCH_CHECK(cos_t.scalar_type() == at::kFloat && sin_t.scalar_type() == at::kFloat && cos_t.size(-1) == 64,
+                    "rotary tables: fp32 [positions, 64]");
+        TORCH_CHECK(q_out.is_contiguous() && q_out.numel() == x.size(0) * hq * 128, "q_out: [M, hq, 128]");
+        TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(0) >= x.size(0) && k_cache.size(2) == hkv &&
+                        k_cache.size(3) == 128 && v_cache.sizes() == k_cache.sizes() && k_cache.is_contiguous() &&
+                        v_cache.is_contiguous(),
+                    "KV caches: [batch, max_len, hkv, 128]");
+        TORCH_CHECK(partials.is_cuda() && partials.scalar_type() == at::kFloat &&
+                        partials.numel() >= splits * x.size(0) * w.size(0),
+                    "partials must be a CUDA float32 tensor of splits * M * N elements");
+        TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && counters.numel() >= w.size(0) / 128,
+                    "counters must be a zeroed CUDA int32 tensor of N / 128 elements");
+        const at::cuda::OptionalCUDAGuard guard(device_of(x));
+        b200ar::RopeKvArgs r{};
+        r.pos = pos.data_ptr<int>();
+        r.cos_t = cos_t.data_ptr<float>();
+        r.sin_t = sin_t.data_ptr<float>();
+        r.q_out = static_cast<__nv_bfloat16*>(q_out.data_ptr());
+        r.k_cache = static_cast<__nv_bfloat16*>(k_cache.data_ptr());
+        r.v_cache = static_cast<__nv_bfloat16*>(v_cache.data_ptr());
+        r.hq = hq;
+        r.hkv = hkv;
+        r.max_len = static_cast<int>(k_cache.size(1));
+        b200ar::gemm_skinny(x.data_ptr(), w.data_ptr(), nullptr, partials.data_ptr<float>(),
+                            reinterpret_cast<unsigned*>(counters.data_ptr<int>()), x.size(0), w.size(0), x.size(1),
+                            splits, err.data_ptr<int>(), at::cuda::getCurrentCUDAStream().stream(), 2, &r);
+      },
+      "decode QKV GEMM (M <= 128) with RoPE and the KV-cache write in its split-K epilogue", py::arg("x"),
+      py::arg("w"), py::arg("pos"), py::arg("cos_t"), py::arg("sin_t"), py::arg("q_out"), py::arg("k_cache"),
+      py::arg("v_cache"), py::arg("partials"), py::arg("counters"), py::arg("err"), py::arg("splits"),
+      py::arg("hq"), py::arg("hkv"));
 }

@@ -82,13 +82,14 @@ void rmsnorm_cuda(const at::Tensor& x, const at::Tensor& gamma, double eps, cons
           static_cast<float>(eps), current_stream());
 }
 
-void silu_mul_cuda(const at::Tensor& gate_up, const at::Tensor& y) {
+void silu_mul_cuda(const at::Tensor& gate_up, const at::Tensor& y, int64_t group) {
   TORCH_CHECK(gate_up.is_cuda() && gate_up.dim() == 2 && gate_up.is_contiguous() && y.is_contiguous() &&
                   gate_up.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16,
               "b200ar::silu_mul takes contiguous bf16 CUDA tensors");
   TORCH_CHECK(gate_up.size(1) % 2 == 0 && y.numel() == gate_up.numel() / 2, "shape mismatch");
   const c10::cuda::CUDAGuard guard(gate_up.device());
-  silu_mul(gate_up.data_ptr(), y.data_ptr(), gate_up.size(0), gate_up.size(1) / 2, current_stream());
+  silu_mul(gate_up.data_ptr(), y.data_ptr(), gate_up.size(0), gate_up.size(1) / 2, current_stream(),
+           static_cast<int>(group));
 }
 
 // Meta (fake) implementations: outputs are caller-provided, nothing to compute.
@@ -104,7 +105,7 @@ void ar_rmsnorm_meta(int64_t, const at::Tensor& x, const at::Tensor& residual, c
 void rmsnorm_meta(const at::Tensor& x, const at::Tensor& gamma, double, const at::Tensor& y) {
   TORCH_CHECK(gamma.numel() > 0 && x.numel() % gamma.numel() == 0 && y.numel() == x.numel(), "shape mismatch");
 }
-void silu_mul_meta(const at::Tensor& gate_up, const at::Tensor& y) {
+void silu_mul_meta(const at::Tensor& gate_up, const at::Tensor& y, int64_t) {
   TORCH_CHECK(gate_up.dim() == 2 && gate_up.size(1) % 2 == 0 && y.numel() == gate_up.numel() / 2, "shape mismatch");
 }
 
@@ -117,7 +118,7 @@ TORCH_LIBRARY(b200ar, m) {
       "all_reduce_residual_rmsnorm(int comm, Tensor x, Tensor residual, Tensor gamma, float eps, Tensor(a!) y, "
       "Tensor(b!) residual_out, int variant=0, int ctas=0) -> ()");
   m.def("rmsnorm(Tensor x, Tensor gamma, float eps, Tensor(a!) y) -> ()");
-  m.def("silu_mul(Tensor gate_up, Tensor(a!) y) -> ()");
+  m.def("silu_mul(Tensor gate_up, Tensor(a!) y, int group=0) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(b200ar, CUDA, m) {

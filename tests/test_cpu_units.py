@@ -5,6 +5,7 @@ import json
 import pickle
 
 import pytest
+import torch
 
 
 def test_build_table_merges_and_covers_everything():
@@ -289,3 +290,15 @@ def test_bench_summary_rows_and_crossover():
     assert cross["crossover_band_bytes"]["eager"] == []
     sweep1, _, cross1 = bench.summarize({f"eager/{s}": [5.0] for s in sizes}, sizes, 1, str, False, False, False)
     assert cross1 == {} and "busbw_gbs" not in sweep1[0] and "graph_p50_us" not in sweep1[0]
+
+
+def test_split_gate_up_layouts():
+    from b200ar.ops.layers import ref_silu_mul, split_gate_up
+
+    gu = torch.arange(2 * 256, dtype=torch.float32).view(2, 256)
+    g, u = split_gate_up(gu, 64)
+    assert torch.equal(g[0, :64], torch.arange(64.0)) and torch.equal(u[0, :64], torch.arange(64.0, 128.0))
+    assert torch.equal(g[1, 64:], torch.arange(256 + 128, 256 + 192.0))
+    g0, u0 = split_gate_up(gu, 0)
+    assert torch.equal(g0, gu[:, :128]) and torch.equal(u0, gu[:, 128:])
+    assert ref_silu_mul(gu.to(torch.bfloat16), 64).shape == (2, 128)

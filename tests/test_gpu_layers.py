@@ -84,3 +84,11 @@ def test_decode_attention_merge_rearms(splits):
         torch.cuda.synchronize()
         ref = ref_decode_attention(q, kc, vc, seq, hq, hkv)
         torch.testing.assert_close(out.float()[:3], ref[:3], atol=2e-2, rtol=2e-2)
+
+
+def test_silu_mul_interleaved_groups():
+    from b200ar.ops.layers import ref_silu_mul, silu_mul
+
+    gu = torch.randn(5, 2 * 1024, device="cuda").to(torch.bfloat16)
+    torch.testing.assert_close(silu_mul(gu, group=64).float(), ref_silu_mul(gu, group=64).float(), atol=2e-2,
+                               rtol=1e-2)
