@@ -25,7 +25,8 @@ _ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 def build_inplace(verbose: bool = False) -> None:
     """Compiles every native source for sm_100a into ``b200ar/_C*.so`` (the
     checked build when ``B200AR_CHECKS=1`` is in the environment)."""
-    lock_path = os.path.join(_ROOT, ".b200ar_build.lock")
+    os.makedirs(os.path.join(_ROOT, "build"), exist_ok=True)
+    lock_path = os.path.join(_ROOT, "build", ".b200ar_build.lock")
     with open(lock_path, "w") as lock:
         fcntl.flock(lock, fcntl.LOCK_EX)
         env = dict(os.environ)

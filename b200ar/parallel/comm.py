@@ -58,6 +58,7 @@ class CustomAllreduce:
         self._peer_ptrs: List[int] = []
         self._ws_ptr = 0
         self.nvls = None
+        self._fast = None  # bound Comm.all_reduce_auto once the CUDA communicator exists
 
         # Slot capacity: two-shot of max_size, or one-shot push of push_max_size.
         cap = max(
@@ -152,6 +153,7 @@ class CustomAllreduce:
         self.selector = list(entries)
         if self._comm is not None:
             self._comm.set_selector(sel.to_native(self.selector))
+            self._fast = self._comm.all_reduce_auto if self.cfg.variant == "auto" else None
 
     def plan(self, nbytes: int, variant="auto", ctas: int = 0):
         """(variant name, ctas, threads) that a message of ``nbytes`` would use."""
@@ -202,10 +204,15 @@ class CustomAllreduce:
         on a 16-byte boundary run on the b200ar kernels (or NCCL above the
         measured crossover). Other tensors go to NCCL when an NCCL group is
         available, else through a zero-padded contiguous copy."""
-        if self.closed:
-            raise RuntimeError("communicator is closed")
         if out is None:
             out = torch.empty_like(inp)
+        fast = self._fast
+        if fast is not None and variant == "auto" and not ctas and not torch.compiler.is_compiling():
+            # Lean eager path: dtype/layout/alignment checks, plan and launch in one native call.
+            if fast(inp, out):
+                return out
+        if self.closed:
+            raise RuntimeError("communicator is closed")
         v = sel.variant_id(variant if variant != "auto" else self.cfg.variant)
         if torch.compiler.is_compiling() and self._handle:
             # Traced by torch.compile: one dispatcher op, no host-side fallback
@@ -417,6 +424,7 @@ class CustomAllreduce:
         if self.closed:
             return
         self.closed = True
+        self._fast = None
         if self._comm is not None:
             torch.cuda.synchronize(self.device)
         if dist.is_initialized():

@@ -8,7 +8,8 @@ One step = one all-reduce of every size in eager mode and one graph replay of
 every size, each preceded by an L2 flush (a 256 MiB write) and timed with its
 own pair of CUDA events; our arm also times NCCL the same way. Per-call times
 are reduced with a MAX over ranks, then p50 over the K steps. ``value`` is the
-geometric mean over sizes of the eager p50 (µs, lower is better). ``e2e`` times
+geometric mean over sizes of the eager p50 (µs, lower is better); the line ends
+with compact per-size ``rows`` (columns ``rows_cols``). ``e2e`` times
 the public API end to end on the host clock: H2D copy of the input from pinned
 memory, all-reduce, D2H copy of the result, synchronize.
 
@@ -94,11 +95,11 @@ class OursArm:
         sys.path.insert(0, ROOT)
         from b200ar import CustomAllreduce
 
-        # NVLS (switch reduction) pays off from 4 ranks up; its multicast
-        # buffer is released in close() before the process ends.
-
+        # No NVLS multicast buffer: the selector tables never pick NVLS, and a
+        # rank that died with memory bound to a multicast object would fault
+        # its peers' GPUs.
         self.comm = CustomAllreduce(group=gloo, device=torch.device("cuda", torch.cuda.current_device()),
-                                    nccl_group=dist.group.WORLD, max_size=max_bytes, enable_nvls=world > 2)
+                                    nccl_group=dist.group.WORLD, max_size=max_bytes, enable_nvls=False)
 
     def all_reduce(self, inp, out):
         self.comm.all_reduce(inp, out)
@@ -268,6 +269,21 @@ def summarize(per_call, sz_list, world, variant_of, graphs_on, nccl_on, nccl_gra
     return sweep, value, cross
 
 
+ROW_COLS = ["bytes", "variant", "eager_p50_us", "graph_p50_us", "nccl_eager_p50_us", "nccl_graph_p50_us",
+            "e2e_p50_us"]
+
+
+def compact_rows(sweep, e2e_p50=None):
+    """One short list per size (columns ``ROW_COLS``; None where a mode did not
+    run), so that every size fits in the tail of the printed line."""
+    rows = []
+    for r in sweep:
+        e = (e2e_p50 or {}).get(r["bytes"])
+        rows.append([r["bytes"], r["variant"]] + [r.get(k) for k in ROW_COLS[2:6]] +
+                    [round(e, 2) if e is not None else None])
+    return rows
+
+
 def run(args):
     sys.path.insert(0, ROOT)
     from b200ar.utils.clocks import ClockSampler
@@ -341,7 +357,7 @@ def run(args):
     clocks = sampler.summary() if local == 0 else {}
 
     # ---- end to end through the public API: pinned H2D, all-reduce, D2H ----
-    e2e = None
+    e2e, e2e_p50 = None, None
     if not args.no_e2e:
         host_in = {s: inps[s].cpu().pin_memory() for s in sz_list}
         host_out = {s: torch.empty_like(host_in[s]).pin_memory() for s in sz_list}
@@ -365,7 +381,6 @@ def run(args):
             "unit": "us (geomean over sizes of p50, host clock, max over ranks)",
             "h2d_bytes_per_step": int(sum(sz_list)),
             "d2h_bytes_per_step": int(sum(sz_list)),
-            "per_size_p50_us": {str(s): round(v, 2) for s, v in e2e_p50.items()},
         }
 
     sweep, value, cross = summarize(per_call, sz_list, world, arm.variant, bool(graphs), with_nccl,
@@ -395,27 +410,27 @@ def run(args):
         "impl": arm.name,
         "gpu_launches": int(launches),
         "clocks": clocks,
-        "sweep": sweep,
     }
     result.update(cross)
     if e2e:
         result["e2e"] = e2e
+    # Per-size rows last and compact, so that the end of the line (what a
+    # log tail keeps) holds every size; p10/p90/max and bandwidths go to --json-out.
+    result["rows_cols"] = ROW_COLS
+    result["rows"] = compact_rows(sweep, e2e_p50)
     arm.close()
     if rank == 0:
-        line = json.dumps(result)
-        print(line, flush=True)
+        print(json.dumps(result), flush=True)
         if args.json_out:
             with open(args.json_out, "w") as f:
-                f.write(line + "\n")
-    # Graphs that captured NCCL calls can make process-group teardown hang, so
-    # drop them first and leave without destroying the NCCL communicator.
+                f.write(json.dumps(dict(result, sweep=sweep)) + "\n")
+    # Orderly teardown: captured graphs first (some hold NCCL work), then the
+    # device, then the process groups; the interpreter then exits normally.
     graphs.clear()
     nccl_graphs.clear()
     torch.cuda.synchronize()
     dist.barrier(group=gloo)
-    sys.stdout.flush()
-    sys.stderr.flush()
-    os._exit(0)
+    dist.destroy_process_group()
 
 
 def main():

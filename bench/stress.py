@@ -44,6 +44,13 @@ HIDDEN = 7168
 LAYERS = 61
 
 
+def make_sync(on_gpu: bool):
+    """Waits for the device's queued work on GPU ranks; nothing to wait for on CPU ranks."""
+    if on_gpu:
+        return torch.cuda.synchronize
+    return lambda: None
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--random-iters", type=int, default=100000)
@@ -68,9 +75,7 @@ def main():
         dev = torch.device("cpu")
         comm = CustomAllreduce(group=gloo, device=dev, max_size=max(args.max_random_bytes, 1 << 20))
 
-    def sync():
-        if on_gpu:
-            sync()
+    sync = make_sync(on_gpu)
     ws = world
     tri = ws * (ws + 1) / 2.0
     results = {}
@@ -272,8 +277,9 @@ def main():
         print(f"\n{'ALL STRESS TESTS PASSED' if ok else 'SOME STRESS TESTS FAILED'}", flush=True)
     sync()
     dist.barrier(group=gloo)
+    dist.destroy_process_group()
     sys.stdout.flush()
-    os._exit(0 if ok else 1)
+    sys.exit(0 if ok else 1)
 
 
 if __name__ == "__main__":

@@ -135,6 +135,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_ar_slot_bytes", &gemm_ar_slot_bytes);
   m.def("lamport_bytes", &lamport_bytes);
   m.def("workspace_bytes", &workspace_bytes, "bytes of one rank's workspace for a slot capacity");
+  m.def("plan_ctas", &plan_ctas, "CTA count of a collective launch (clamped to the co-resident count)",
+        py::arg("variant"), py::arg("bytes"), py::arg("world"), py::arg("requested"), py::arg("resident"));
   m.def("variant_slot_bytes", &variant_slot_bytes, "slot bytes a variant needs", py::arg("variant"),
         py::arg("bytes"), py::arg("world"));
 
@@ -180,6 +182,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_property_readonly("ptr", [](Communicator& c) { return reinterpret_cast<int64_t>(&c); })
       .def_property_readonly("slot_capacity", &Communicator::slot_capacity)
       .def_property_readonly("launches", &Communicator::launches)
+      .def("resident_ctas", &Communicator::resident_ctas, py::arg("variant"))
       .def_property_readonly("pending_graph_buffers", &Communicator::pending_graph_buffers)
       .def("open_ipc_handle",
            [](Communicator& c, py::bytes h) { return reinterpret_cast<int64_t>(c.open_ipc_handle(h)); })
@@ -229,6 +232,29 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
              return li.variant;
            },
            py::arg("inp"), py::arg("out"), py::arg("variant") = 0, py::arg("ctas") = 0)
+      // Lean eager entry used by CustomAllreduce.all_reduce for variant "auto":
+      // every check in C++, one call from Python. Returns false (nothing
+      // launched) when the Python layer must serve the call instead: a dtype,
+      // layout or alignment the kernels do not take, or the NCCL range.
+      .def("all_reduce_auto",
+           [](Communicator& c, const at::Tensor& inp, const at::Tensor& out) {
+             const auto st = inp.scalar_type();
+             if (st != at::kBFloat16 && st != at::kHalf && st != at::kFloat) return false;
+             if (out.scalar_type() != st || out.numel() != inp.numel()) return false;
+             const int64_t bytes = inp.numel() * inp.element_size();
+             const auto ip = reinterpret_cast<uintptr_t>(inp.data_ptr());
+             const auto op = reinterpret_cast<uintptr_t>(out.data_ptr());
+             if ((bytes | ip | op) & 15) return false;
+             if (!inp.is_cuda() || !inp.is_contiguous() || !out.is_contiguous()) return false;
+             const c10::DeviceIndex dev = inp.device().index();
+             if (out.device() != inp.device()) return false;
+             const at::cuda::OptionalCUDAGuard guard(c10::cuda::current_device() == dev ? std::nullopt
+                                                                                        : std::optional<c10::Device>(inp.device()));
+             cudaStream_t s = at::cuda::getCurrentCUDAStream(dev).stream();
+             LaunchInfo li = c.allreduce(s, inp.data_ptr(), out.data_ptr(), bytes, to_dtype(inp), kAuto, 0);
+             return li.variant != kNccl;
+           },
+           py::arg("inp"), py::arg("out"))
       .def("ar_rmsnorm",
            [](Communicator& c, at::Tensor& x, at::Tensor& residual, at::Tensor& gamma, at::Tensor& y,
               at::Tensor& residual_out, double eps, int variant, int ctas) {

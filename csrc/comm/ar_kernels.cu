@@ -68,6 +68,47 @@ void launch_copy(const void* in, void* out, int64_t packets, cudaStream_t stream
   B200AR_CUDA(cudaGetLastError());
 }
 
+namespace {
+template <typename T, int N>
+const void* kernel_of(int variant) {
+  switch (variant) {
+    case kOneshotPush: return reinterpret_cast<const void*>(&oneshot_push_kernel<T, N>);
+    case kOneshotPull: return reinterpret_cast<const void*>(&oneshot_pull_kernel<T, N>);
+    case kTwoshot: return reinterpret_cast<const void*>(&twoshot_kernel<T, N>);
+    case kRegistered: return reinterpret_cast<const void*>(&registered_kernel<T, N>);
+    case kLamport: return reinterpret_cast<const void*>(&oneshot_lamport_kernel<T, N>);
+    default: return nullptr;
+  }
+}
+
+template <typename T>
+const void* kernel_of_world(int variant, int world) {
+  switch (world) {
+    case 2: return kernel_of<T, 2>(variant);
+    case 3: return kernel_of<T, 3>(variant);
+    case 4: return kernel_of<T, 4>(variant);
+    case 5: return kernel_of<T, 5>(variant);
+    case 6: return kernel_of<T, 6>(variant);
+    case 7: return kernel_of<T, 7>(variant);
+    case 8: return kernel_of<T, 8>(variant);
+    default: return nullptr;
+  }
+}
+}  // namespace
+
+int ar_blocks_per_sm(int variant, DType dt, int world) {
+  const void* k = nullptr;
+  switch (dt) {
+    case DType::kFloat32: k = kernel_of_world<float>(variant, world); break;
+    case DType::kFloat16: k = kernel_of_world<__half>(variant, world); break;
+    case DType::kBFloat16: k = kernel_of_world<__nv_bfloat16>(variant, world); break;
+  }
+  if (k == nullptr) return kMaxCTAs;  // no barrier kernel: no limit from this module
+  int n = 0;
+  B200AR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kArThreads, 0));
+  return n;
+}
+
 void launch_ar_kernel(int variant, DType dt, int world, int ctas, int threads, const ArArgs& a,
                       cudaStream_t stream) {
   if (ctas < 1 || ctas > kMaxCTAs) throw std::invalid_argument("bad CTA count " + std::to_string(ctas));

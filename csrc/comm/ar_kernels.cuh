@@ -310,19 +310,24 @@ B200AR_DEV uint32_t lamport_clean(uint32_t w) {
 template <typename T, int N>
 __global__ void __launch_bounds__(kArThreads) oneshot_lamport_kernel(ArArgs a) {
   __shared__ uint32_t s_gen;
-  const uint32_t gen = read_generation(a.ctx, &s_gen);
   const int r = a.ctx.rank;
   const int64_t P = a.packets;
   const int64_t b = part_begin(P, gridDim.x, blockIdx.x);
   const int64_t e = part_begin(P, gridDim.x, blockIdx.x + 1);
+  // The first input packet is loaded before the generation so that the two
+  // cold loads overlap (decode-size messages have one packet per thread).
+  const int64_t i0 = b + threadIdx.x;
+  uint4 first = make_uint4(0u, 0u, 0u, 0u);
+  if (i0 < e) first = ld_in(a.in + i0 * 16);
+  const uint32_t gen = read_generation(a.ctx, &s_gen);
   const int64_t buf_off = static_cast<int64_t>(gen % kLamportBuffers) * N * a.lam_cap;
   B200AR_ENTRY_RANGE(P * 16, a.lam_cap, 2u)
 
   char* dst[N];
   rotate_ptrs<N>(a.lam, r, dst);
   const int64_t my_off = buf_off + static_cast<int64_t>(r) * a.lam_cap;
-  for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) {
-    uint4 v = ld_in(a.in + i * 16);
+  for (int64_t i = i0; i < e; i += blockDim.x) {
+    uint4 v = i == i0 ? first : ld_in(a.in + i * 16);
     v.x = lamport_clean<T>(v.x);
     v.y = lamport_clean<T>(v.y);
     v.z = lamport_clean<T>(v.z);
@@ -375,6 +380,9 @@ void launch_ar_kernel(int variant, DType dt, int world, int ctas, int threads, c
                       cudaStream_t stream);
 // Fills a device range with the Lamport marker.
 void launch_lamport_init(void* p, int64_t bytes, cudaStream_t stream);
+// Occupancy (resident CTAs per SM at kArThreads threads) of a variant's kernel.
+int ar_blocks_per_sm(int variant, DType dt, int world);
+int nvls_blocks_per_sm(DType dt, int world);
 // World size 1: out = in (16-byte packets) with a b200ar kernel.
 void launch_copy(const void* in, void* out, int64_t packets, cudaStream_t stream);
 }  // namespace b200ar

@@ -271,17 +271,44 @@ LaunchInfo Communicator::plan(int64_t bytes, int variant, int ctas, bool capturi
     }
   }
   li.variant = v;
-  if (v == kOneshotPush || v == kOneshotPull || v == kRegistered || v == kLamport) {
-    const int64_t packets = bytes / 16;
-    const int64_t want = (packets + 2 * kArThreads - 1) / (2 * kArThreads);
-    li.ctas = c > 0 ? c : static_cast<int>(std::clamp<int64_t>(want, 1, 148));
-  } else if (v == kTwoshot || v == kNvls) {
-    const int64_t part = bytes / 16 / world_;
-    const int64_t want = (part + kArThreads - 1) / kArThreads;
-    li.ctas = c > 0 ? c : static_cast<int>(std::clamp<int64_t>(want, 1, 2 * 148));
-  }
-  li.ctas = std::min(li.ctas, kMaxCTAs);
+  li.ctas = plan_ctas(v, bytes, world_, c, resident_ctas(v));
   return li;
+}
+
+int plan_ctas(int variant, int64_t bytes, int world, int requested, int resident) {
+  int64_t want = 0;
+  if (variant == kOneshotPush || variant == kOneshotPull || variant == kRegistered || variant == kLamport) {
+    const int64_t packets = bytes / 16;
+    want = (packets + 2 * kArThreads - 1) / (2 * kArThreads);
+  } else if (variant == kTwoshot || variant == kNvls) {
+    const int64_t part = bytes / 16 / std::max(world, 1);
+    want = (part + kArThreads - 1) / kArThreads;
+  } else {
+    return 0;  // copy / NCCL: not a barrier kernel of this module
+  }
+  int64_t c = requested > 0 ? requested : want;
+  // CTA j of every rank waits for CTA j of its peers, so all CTAs of a launch
+  // must be able to run at once: never more than fit on the device together.
+  c = std::min<int64_t>(c, std::max(resident, 1));
+  return static_cast<int>(std::clamp<int64_t>(c, 1, kMaxCTAs));
+}
+
+int Communicator::resident_ctas(int variant) const {
+  if (variant < 0 || variant >= kNumVariants) return kMaxCTAs;
+  int& cached = resident_[variant];
+  if (cached == 0) {
+    int dev = 0, sms = 0;
+    B200AR_CUDA(cudaGetDevice(&dev));
+    B200AR_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    // The smallest per-SM occupancy over the three dtypes (they differ in registers).
+    int per_sm = INT32_MAX;
+    for (DType dt : {DType::kFloat32, DType::kFloat16, DType::kBFloat16}) {
+      const int b = variant == kNvls ? nvls_blocks_per_sm(dt, world_) : ar_blocks_per_sm(variant, dt, world_);
+      per_sm = std::min(per_sm, b);
+    }
+    cached = std::max(1, per_sm) * sms;
+  }
+  return cached;
 }
 
 LaunchInfo Communicator::allreduce(cudaStream_t stream, const void* in, void* out, int64_t bytes, DType dt,

@@ -69,6 +69,14 @@ struct SelectorEntry {
   int ctas;
 };
 
+// CTA count of a collective launch: `requested` (> 0) or one derived from the
+// size, never above `resident` (the CTAs of that kernel that fit on the device
+// at once; ranks wait on each other's CTAs, so all of them must run together)
+// nor kMaxCTAs. 0 for variants that are not barrier kernels (copy, NCCL).
+int plan_ctas(int variant, int64_t bytes, int world, int requested, int resident);
+
+constexpr int kNumVariants = 9;
+
 struct LaunchInfo {
   int variant = kAuto;
   int ctas = 0;
@@ -141,6 +149,10 @@ class Communicator {
   // identical on every rank).
   LaunchInfo plan(int64_t bytes, int variant, int ctas, bool capturing, bool registered_input) const;
 
+  // CTAs of `variant`'s kernel that can be resident on this device at once
+  // (occupancy x SM count, smallest over dtypes; cached).
+  int resident_ctas(int variant) const;
+
   // --- status ----------------------------------------------------------------
   // Throws CommTimeout if a kernel recorded an error.
   void check_status() const;
@@ -177,6 +189,7 @@ class Communicator {
   std::vector<SelectorEntry> selector_;
   uint64_t launches_ = 0;
   NvlsBuffer* nvls_ = nullptr;
+  mutable int resident_[kNumVariants] = {};
   char* lam_[kMaxRanks] = {};
   int64_t lam_cap_ = 0;
 

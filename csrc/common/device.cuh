@@ -187,6 +187,11 @@ B200AR_DEV uint32_t read_generation(const CommCtx& c, uint32_t* s_gen) {
 // finish advances the generation for the next call on this stream.
 B200AR_DEV void finish_generation(const CommCtx& c, uint32_t gen) {
   __syncthreads();
+  if (gridDim.x == 1) {
+    // One CTA: no arrival count needed (saves an atomic round trip to L2).
+    if (threadIdx.x == 0) c.self->gen = gen + 1u;
+    return;
+  }
   if (threadIdx.x == 0) {
     const uint32_t prev = atomicAdd(&c.self->done, 1u);
     if (prev == gridDim.x - 1) {

@@ -650,10 +650,11 @@ extern "C" int b200ar_residual_rmsnorm_noalloc(const void* x, const void* residu
   using namespace b200ar;
   if (rows < 1 || hidden < 8 || hidden % 8 != 0 || hidden > 16384)
     return noalloc_fail(1, "hidden must be a multiple of 8 in [8, 16384] and rows >= 1");
-  if (rows * hidden * 2 > kNoallocSlot)
-    return noalloc_fail(1, "rows * hidden * 2 = " + std::to_string(rows * hidden * 2) +
-                               " bytes exceeds the allocation-free limit of " + std::to_string(kNoallocSlot) +
-                               " bytes");
+  // Divide before multiplying: a huge `rows` must not wrap around and pass.
+  if (rows > kNoallocSlot / (hidden * 2))
+    return noalloc_fail(1, "rows * hidden * 2 (rows = " + std::to_string(rows) + ", hidden = " +
+                               std::to_string(hidden) + ") exceeds the allocation-free limit of " +
+                               std::to_string(kNoallocSlot) + " bytes");
   for (const void* p : {x, residual, gamma, static_cast<const void*>(y), static_cast<const void*>(residual_out)})
     if (p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 != 0)
       return noalloc_fail(1, "all tensors must be non-null and 16-byte aligned");

@@ -13,7 +13,8 @@
 //    residual_out = x + residual, bf16, row-major [rows, hidden];
 //  * rows * hidden * 2 bytes must not exceed B200AR_NOALLOC_MAX_BYTES (2 MiB),
 //    hidden a multiple of 8 and at most 16384; larger requests are rejected;
-//  * the scratch array (B200AR_NOALLOC_SCRATCH_BYTES per GPU) stays resident
+//  * the scratch array (b200ar_noalloc_scratch_bytes() per GPU: a 16.3 KiB
+//    signal block plus two slots of B200AR_NOALLOC_MAX_BYTES) stays resident
 //    on every GPU that loads the library until the process exits;
 //  * the first call on a device sets up that device (looks up the array's
 //    device address and clears its signal block); make that first call before

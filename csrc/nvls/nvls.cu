@@ -278,6 +278,30 @@ void NvlsBuffer::bind_and_map() {
   B200AR_CUDA(cudaMemset(reinterpret_cast<void*>(uc_va_), 0, static_cast<size_t>(bytes_)));
 }
 
+int nvls_blocks_per_sm(DType dt, int world) {
+  const void* k = nullptr;
+  auto pick = [&](auto tag) {
+    using T = decltype(tag);
+    switch (world) {
+      case 2: k = reinterpret_cast<const void*>(&nvls_kernel<T, 2>); break;
+      case 3: k = reinterpret_cast<const void*>(&nvls_kernel<T, 3>); break;
+      case 4: k = reinterpret_cast<const void*>(&nvls_kernel<T, 4>); break;
+      case 5: k = reinterpret_cast<const void*>(&nvls_kernel<T, 5>); break;
+      case 6: k = reinterpret_cast<const void*>(&nvls_kernel<T, 6>); break;
+      case 7: k = reinterpret_cast<const void*>(&nvls_kernel<T, 7>); break;
+      case 8: k = reinterpret_cast<const void*>(&nvls_kernel<T, 8>); break;
+      default: break;
+    }
+  };
+  if (dt == DType::kFloat32) pick(float{});
+  else if (dt == DType::kFloat16) pick(__half{});
+  else pick(__nv_bfloat16{});
+  if (k == nullptr) return kMaxCTAs;
+  int n = 0;
+  B200AR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kArThreads, 0));
+  return n;
+}
+
 void nvls_allreduce(Communicator& comm, NvlsBuffer& buf, cudaStream_t stream, const void* in, void* out,
                     int64_t bytes, int dtype, int ctas) {
   comm.check_status();
@@ -294,8 +318,8 @@ void nvls_allreduce(Communicator& comm, NvlsBuffer& buf, cudaStream_t stream, co
   a.packets = bytes / 16;
   const int world = comm.world();
   const int64_t part = a.packets / world;
-  int grid = ctas > 0 ? ctas : static_cast<int>(std::clamp<int64_t>((part + kArThreads - 1) / kArThreads, 1, 2 * 148));
-  grid = std::min(grid, kMaxCTAs);
+  (void)part;
+  const int grid = plan_ctas(kNvls, bytes, world, ctas, comm.resident_ctas(kNvls));
   switch (dtype) {
     case 0: launch_t<float>(world, grid, a, stream); break;
     case 1: launch_t<__half>(world, grid, a, stream); break;

@@ -21,3 +21,18 @@ def test_stress_suite_cpu_two_ranks():
     assert "ALL STRESS TESTS PASSED" in res.stdout, out[-4000:]
     for name in ("rapid_fire", "unique_values", "back_to_back", "continuous_batching", "random_sizes"):
         assert f"{name}" in res.stdout and "FAIL" not in res.stdout
+
+
+def test_stress_sync_helpers_do_not_recurse():
+    """The GPU branch's sync helper must be the device synchronize itself (a
+    helper that called itself once made every GPU scenario fail at its first
+    sync); the CPU one must return without waiting."""
+    import importlib.util
+
+    import torch
+
+    spec = importlib.util.spec_from_file_location("stress_main", os.path.join(ROOT, "bench", "stress.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    assert mod.make_sync(True) is torch.cuda.synchronize
+    assert mod.make_sync(False)() is None

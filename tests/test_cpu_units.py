@@ -302,3 +302,35 @@ def test_split_gate_up_layouts():
     g0, u0 = split_gate_up(gu, 0)
     assert torch.equal(g0, gu[:, :128]) and torch.equal(u0, gu[:, 128:])
     assert ref_silu_mul(gu.to(torch.bfloat16), 64).shape == (2, 128)
+
+
+def test_plan_ctas_never_exceeds_coresident_count():
+    """Barrier kernels wait on the same CTA index of every peer, so a launch
+    must never have more CTAs than fit on the device at once."""
+    from b200ar._native import _C
+
+    V = _C.VARIANTS
+    barrier_kernels = ["oneshot_push", "oneshot_pull", "twoshot", "registered", "lamport", "nvls"]
+    sizes = [16, 4096, 1 << 20, 64 << 20, 1 << 30]
+    for name in barrier_kernels:
+        for world in range(2, 9):
+            for resident in (1, 37, 148, 296):
+                for requested in (0, 1, 100, 444, 512):
+                    for nbytes in sizes:
+                        c = _C.plan_ctas(V[name], nbytes, world, requested, resident)
+                        assert 1 <= c <= min(resident, _C.MAX_CTAS), (name, world, resident, requested, nbytes, c)
+                        if requested:
+                            assert c == min(requested, resident)
+    # Large messages want more CTAs than one SM's worth; the clamp decides.
+    assert _C.plan_ctas(V["twoshot"], 1 << 30, 8, 0, 148) == 148
+    assert _C.plan_ctas(V["copy"], 1 << 20, 1, 0, 148) == 0 and _C.plan_ctas(V["nccl"], 1 << 20, 8, 0, 148) == 0
+
+
+def test_bench_compact_rows():
+    bench = _load_bench()
+    sweep = [{"bytes": 4096, "variant": "lamport", "eager_p50_us": 11.0, "graph_p50_us": 9.0,
+              "nccl_eager_p50_us": 20.0, "eager_us": {}},
+             {"bytes": 8192, "variant": "twoshot", "eager_p50_us": 12.0}]
+    rows = bench.compact_rows(sweep, {4096: 40.123})
+    assert bench.ROW_COLS[0] == "bytes" and len(bench.ROW_COLS) == 7
+    assert rows == [[4096, "lamport", 11.0, 9.0, 20.0, None, 40.12], [8192, "twoshot", 12.0, None, None, None, None]]
