@@ -236,14 +236,8 @@ class CustomAllreduce:
             return self._nccl(inp, out)
         launched = self._comm.all_reduce(inp, out, v, ctas)
         if launched == sel.VARIANTS["nccl"]:
-            # torch's NCCL all_reduce is in place: out of place it costs an extra
-            # copy, which the measured crossover (in-place NCCL) did not include.
-            # Out-of-place calls then use the two-shot kernel when it fits.
-            nbytes = inp.numel() * inp.element_size()
-            if (out.data_ptr() != inp.data_ptr() and v == sel.VARIANTS["auto"]
-                    and _C.variant_slot_bytes(sel.VARIANTS["twoshot"], nbytes, self.world) <= self.slot_capacity):
-                self._comm.all_reduce(inp, out, sel.VARIANTS["twoshot"], 0)
-                return out
+            # Above the measured crossover (which was measured on this same
+            # out-of-place NCCL path) or beyond the slot capacity.
             return self._nccl(inp, out)
         return out
 

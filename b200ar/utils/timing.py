@@ -24,16 +24,41 @@ class L2Flusher:
     ``lead_us`` first keeps the GPU busy with a spin kernel so that the host
     has enqueued the timed call (and its events) before the GPU reaches it;
     otherwise a short kernel's event time would include host launch overhead.
+
+    With ``align_group`` (an NCCL group), a one-element NCCL all-reduce runs
+    first, so that every rank's GPU leaves the flush at about the same time:
+    without it, a collective whose ranks finish at different times (a large
+    NCCL call, say) skews the start of the next timed call across ranks, and
+    the next call's time absorbs that skew.
     """
 
-    def __init__(self, device, nbytes: int = L2_FLUSH_BYTES, lead_us: float = 60.0, sm_mhz: float = 1965.0):
+    def __init__(self, device, nbytes: int = L2_FLUSH_BYTES, lead_us: float = 60.0, sm_mhz: float = 1965.0,
+                 align_group=None):
         self.buf = torch.empty(nbytes // 4, dtype=torch.int32, device=device)
         self.cycles = int(lead_us * sm_mhz)
+        self.align_group = align_group
+        self.token = torch.zeros(1, dtype=torch.float32, device=device) if align_group is not None else None
 
     def __call__(self) -> None:
+        if self.align_group is not None:
+            dist.all_reduce(self.token, group=self.align_group)
         if self.cycles:
             torch.cuda._sleep(self.cycles)
         self.buf.fill_(0x5A5A5A5A)
+
+
+def aligned_start(group, lead_s: float = 0.002) -> None:
+    """Host-side start alignment for end-to-end timing: rank 0 picks a
+    deadline ``lead_s`` ahead on the host's monotonic clock (shared by every
+    process on the node) and each rank busy-waits until it passes, so ranks
+    start their timed region within a few microseconds of each other instead
+    of the tens of microseconds a barrier's release leaves between them."""
+    import time
+
+    t = [time.monotonic() + lead_s if dist.get_rank(group) == 0 else 0.0]
+    dist.broadcast_object_list(t, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+    while time.monotonic() < t[0]:
+        pass
 
 
 class EventTimer:

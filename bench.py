@@ -56,21 +56,6 @@ def sizes(lo, hi):
     return out
 
 
-@contextlib.contextmanager
-def stdout_to_stderr():
-    """Keeps build logs (the reference JIT-compiles on import) off stdout, which
-    carries exactly one JSON line."""
-    sys.stdout.flush()
-    saved = os.dup(1)
-    os.dup2(2, 1)
-    try:
-        yield
-    finally:
-        sys.stdout.flush()
-        os.dup2(saved, 1)
-        os.close(saved)
-
-
 def init_dist(n):
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -86,6 +71,10 @@ def init_dist(n):
 
 
 # --------------------------------------------------------------------------- arms
+sys.path.insert(0, os.path.join(ROOT, "bench"))
+from reference_arm import ReferenceArm  # noqa: E402  (the unmodified reference through its own API)
+
+
 class OursArm:
     """b200ar through its public API (CustomAllreduce)."""
 
@@ -111,81 +100,10 @@ class OursArm:
         return self.comm.launches
 
     def variant(self, nbytes):
-        v = self.comm.plan(nbytes)[0]
-        # Out-of-place calls above the NCCL crossover run the two-shot kernel.
-        return "twoshot" if v == "nccl" else v
+        return self.comm.plan(nbytes)[0]
 
     def close(self):
         self.comm.close()
-
-
-class ReferenceArm:
-    """The unmodified reference (baseline/_ref/pcie_allreduce) through its own
-    public API, bootstrapped like its bench_crossover.py."""
-
-    name = "reference"
-
-    def __init__(self, rank, world, gloo, max_bytes):
-        ref = os.path.join(ROOT, "baseline", "_ref")
-        if not os.path.isdir(os.path.join(ref, "pcie_allreduce")):
-            raise RuntimeError("reference not installed under baseline/_ref")
-        sys.path.insert(0, ref)
-        with stdout_to_stderr():
-            import pcie_allreduce  # noqa: F401  (JIT build happens here)
-        from pcie_allreduce.cuda_ipc import CudaIPC
-
-        self.ar = pcie_allreduce
-        self.rank, self.world, self.gloo = rank, world, gloo
-        ipc = CudaIPC()
-        cap = max_bytes * world  # push path needs bytes * world <= capacity
-        meta_sz = pcie_allreduce.meta_size()
-        meta = ipc.malloc(meta_sz + cap)
-        ipc.memset(meta, 0, meta_sz + cap)
-        self._refs = []
-
-        def exchange(ptr):
-            hs = [None] * world
-            dist.all_gather_object(hs, ipc.ipc_get_handle(ptr), group=gloo)
-            out = []
-            for i, h in enumerate(hs):
-                if i == rank:
-                    out.append(ptr.value)
-                else:
-                    p = ipc.ipc_open_handle(h)
-                    self._refs.append(p)
-                    out.append(p.value)
-            return out
-
-        meta_ptrs = exchange(meta)
-        buf0 = exchange(ipc.malloc(cap))
-        buf1 = exchange(ipc.malloc(cap))
-        self.rank_data = torch.empty(8 << 20, dtype=torch.uint8, device="cuda")
-        self.fa = pcie_allreduce.init_custom_ar(meta_ptrs, self.rank_data, rank)
-        pcie_allreduce.register_pcie_buffers(self.fa, buf0, buf1, cap)
-        torch.cuda.synchronize()
-        dist.barrier(group=gloo)
-        self.n = 0
-
-    def all_reduce(self, inp, out):
-        self.ar.all_reduce(self.fa, inp, out, 0, 0)
-        self.n += 1
-
-    def post_capture(self):
-        handle, off = self.ar.get_graph_buffer_ipc_meta(self.fa)
-        meta = [None] * self.world
-        dist.all_gather_object(meta, (handle, off), group=self.gloo)
-        self.ar.register_graph_buffers(self.fa, [m[0] for m in meta], [m[1] for m in meta])
-        dist.barrier(group=self.gloo)
-
-    def launches(self):
-        return self.n  # one kernel per call (cu:425-476)
-
-    def variant(self, nbytes):
-        return "reference"
-
-    def close(self):
-        torch.cuda.synchronize()
-        dist.barrier(group=self.gloo)
 
 
 # --------------------------------------------------------------------------- measurement
@@ -287,7 +205,7 @@ def compact_rows(sweep, e2e_p50=None):
 def run(args):
     sys.path.insert(0, ROOT)
     from b200ar.utils.clocks import ClockSampler
-    from b200ar.utils.timing import EventTimer, L2Flusher, geomean, max_over_ranks, percentile
+    from b200ar.utils.timing import EventTimer, L2Flusher, aligned_start, geomean, max_over_ranks, percentile
 
     rank, world, local, gloo = init_dist(args.gpus)
     dev = torch.device("cuda", local)
@@ -295,7 +213,7 @@ def run(args):
     arm = (OursArm if args.impl == "b200ar" else ReferenceArm)(rank, world, gloo, args.max_bytes)
     inps, outs = make_inputs(sz_list, rank, dev)
     validate(arm, inps, outs, sz_list)
-    flush = L2Flusher(dev)
+    flush = L2Flusher(dev, align_group=dist.group.WORLD if world > 1 else None)
     with_nccl = args.impl == "b200ar" and world > 1
     nccl_bufs = {s: inps[s].clone() for s in sz_list} if with_nccl else {}
 
@@ -367,7 +285,8 @@ def run(args):
             for s in sz_list:
                 flush()
                 torch.cuda.synchronize()
-                dist.barrier(group=gloo)
+                if world > 1:
+                    aligned_start(gloo)
                 t = time.perf_counter()
                 dev_in[s].copy_(host_in[s], non_blocking=True)
                 arm.all_reduce(dev_in[s], outs[s])
@@ -406,6 +325,8 @@ def run(args):
             "sizes_bytes": [sz_list[0], sz_list[-1]],
             "modes": ["eager"] + (["graph"] if graphs else []),
             "l2": "flushed (256 MiB write) before every timed call",
+            "alignment": "one-element NCCL all-reduce before each flush (device); e2e starts at a shared "
+                         "host-clock deadline (host)",
         },
         "impl": arm.name,
         "gpu_launches": int(launches),

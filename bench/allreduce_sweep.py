@@ -50,7 +50,7 @@ def main():
     comm = CustomAllreduce(group=gloo, device=dev, nccl_group=dist.group.WORLD, max_size=args.max_bytes,
                            push_max_size=max(1 << 20, args.max_bytes // 16), lamport_max_size=4 << 20,
                            enable_nvls=args.nvls)
-    flush = L2Flusher(dev)
+    flush = L2Flusher(dev, align_group=dist.group.WORLD)
 
     sizes = []
     b = args.min_bytes
@@ -72,12 +72,15 @@ def main():
             if v == "nvls" and (comm.nvls is None or s > comm.nvls.bytes):
                 continue
             per = packets // world if v in ("twoshot", "nvls") else packets
+            resident = comm._comm.resident_ctas(sel.VARIANTS[v])
             for ctas in args.ctas:
                 if ctas > 1 and per // ctas < 32:
                     continue
-                if ctas > 512:
+                if ctas > min(512, resident):  # the launch would be clamped to the co-resident count
                     continue
                 cands.append((v, ctas))
+        # NCCL as the library runs it out of place (reduce-scatter into the
+        # output's shard + in-place all-gather): what a table entry "nccl" costs.
         cands.append(("nccl", 0))
         timer = EventTimer(pool=2 * len(cands) * args.iters)
         for it in range(args.warmup + args.iters):
@@ -86,7 +89,7 @@ def main():
                 if it >= args.warmup:
                     timer.start(f"{v}/{c}")
                 if v == "nccl":
-                    dist.all_reduce(y)
+                    comm._nccl(x, y)
                 else:
                     comm.all_reduce(x, y, variant=v, ctas=c)
                 if it >= args.warmup:
@@ -121,8 +124,7 @@ def main():
     comm.close()  # releases the NVLS buffer before the process ends
     torch.cuda.synchronize()
     dist.barrier(group=gloo)
-    sys.stdout.flush()
-    os._exit(0)
+    dist.destroy_process_group()
 
 
 def _C_slot(variant, nbytes, world):

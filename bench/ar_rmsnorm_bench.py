@@ -6,6 +6,8 @@ gamma = 1 + 0.01 N(0,1), eps 1e-5. Times (p50 of max over ranks, L2 flushed):
   fused          b200ar one kernel (one-shot push or two-shot by size)
   ours_unfused   b200ar all-reduce, then PyTorch add + RMSNorm
   nccl_torch     NCCL all-reduce, then PyTorch add + RMSNorm
+  ref_torch      the reference's all-reduce kernel (unmodified, its own API),
+                 then PyTorch add + RMSNorm (even world sizes, when installed)
 and the roofline max(all-reduce bytes over NVLink at 770 GB/s, HBM bytes at
 the measured copy bandwidth) for the fused kernel.
 
@@ -27,6 +29,7 @@ sys.path.insert(0, ROOT)
 
 from b200ar import CustomAllreduce  # noqa: E402
 from b200ar.utils.timing import EventTimer, L2Flusher, max_over_ranks, percentile  # noqa: E402
+from reference_arm import ReferenceArm, reference_available  # noqa: E402
 
 NVLINK_GBS = 770.0
 
@@ -56,8 +59,11 @@ def main():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         peaks = json.load(open(p))
-    flush = L2Flusher(dev)
+    flush = L2Flusher(dev, align_group=dist.group.WORLD)
     H, eps = 8192, 1e-5
+    ref = None
+    if world > 1 and world % 2 == 0 and reference_available():
+        ref = ReferenceArm(rank, world, gloo, max(int(t) for t in args.tokens.split(",")) * H * 2)
     g0 = torch.Generator(device=dev).manual_seed(7)
     gamma = (1 + 0.01 * torch.randn(H, generator=g0, device=dev)).to(torch.bfloat16)
     for T in (int(t) for t in args.tokens.split(",")):
@@ -79,11 +85,18 @@ def main():
             zz = (tmp.float() + res.float()).to(torch.bfloat16)
             return torch_norm(zz, gamma, eps), zz
 
+        def unfused_ref():
+            ref.all_reduce(x, tmp)
+            zz = (tmp.float() + res.float()).to(torch.bfloat16)
+            return torch_norm(zz, gamma, eps), zz
+
         impls = {
             "fused": lambda: comm.all_reduce_residual_rmsnorm(x, res, gamma, eps, out=y, residual_out=z),
             "ours_unfused": unfused_ours,
             "nccl_torch": unfused_nccl,
         }
+        if ref is not None:
+            impls["ref_torch"] = unfused_ref
         timer = EventTimer(pool=2 * len(impls) * args.iters)
         for it in range(args.warmup + args.iters):
             for name, fn in impls.items():
@@ -107,9 +120,11 @@ def main():
         if rank == 0:
             print(json.dumps(row), flush=True)
     comm.close()
+    if ref is not None:
+        ref.close()
+    torch.cuda.synchronize()
     dist.barrier(group=gloo)
-    sys.stdout.flush()
-    os._exit(0)
+    dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -2,8 +2,10 @@
 
 8 layers, hidden 8192, 64/8 heads of 128, FFN 28672, KV cache pre-filled with
 2048 random tokens, random-init weights; batch 1 / 8 / 32 / 64; both the
-b200ar step and the plain-PyTorch reference step (cuBLAS + NCCL + PyTorch
-attention) are captured in CUDA graphs and timed with CUDA events (max over
+b200ar step, the plain-PyTorch step (cuBLAS + NCCL + PyTorch attention) and,
+for even world sizes when the reference library is installed, the same
+PyTorch step with the reference's all-reduce kernel in place of NCCL
+(``torch_refar``) are captured in CUDA graphs and timed with CUDA events (max over
 ranks, p50 of replays). Weights (~1.7 GB per rank per step at TP 8) exceed L2.
 
     python -m torch.distributed.run --nproc-per-node N bench/decoder_bench.py
@@ -25,6 +27,7 @@ sys.path.insert(0, ROOT)
 from b200ar import CustomAllreduce  # noqa: E402
 from b200ar.models.llama import LlamaConfig, ReferenceDecoder, TPLlamaDecoder  # noqa: E402
 from b200ar.utils.timing import EventTimer, max_over_ranks, percentile  # noqa: E402
+from reference_arm import ReferenceArm, reference_available  # noqa: E402
 
 
 def step_bytes(model) -> int:
@@ -54,6 +57,10 @@ def main():
     dev = torch.device("cuda", local)
     comm = CustomAllreduce(group=gloo, device=dev, nccl_group=dist.group.WORLD, max_size=16 << 20)
     cfg = LlamaConfig.llama3_70b_slice(args.layers)
+    ref_ar = None
+    if world > 1 and world % 2 == 0 and reference_available():
+        max_b = max(int(b) for b in args.batches.split(","))
+        ref_ar = ReferenceArm(rank, world, gloo, max_b * cfg.hidden * 2)
     peaks = {}
     pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(pk):
@@ -64,8 +71,18 @@ def main():
         model.set_input((torch.randn(B, cfg.hidden, device=dev)).to(torch.bfloat16))
         ours = model.capture()
         ref = ReferenceDecoder(model).capture()
+        arms = [("b200ar", ours), ("torch_nccl", ref)]
+        if ref_ar is not None:
+            tmp = torch.empty(B, cfg.hidden, dtype=torch.bfloat16, device=dev)
+
+            def ref_allreduce(t):  # the reference's API is out of place
+                ref_ar.all_reduce(t, tmp)
+                t.copy_(tmp)
+
+            arms.append(("torch_refar", ReferenceDecoder(model, allreduce=ref_allreduce).capture()))
+            ref_ar.post_capture()
         res = {"batch": B, "world": world, "layers": cfg.layers, "hbm_bytes_per_step": step_bytes(model)}
-        for name, g in (("b200ar", ours), ("torch_nccl", ref)):
+        for name, g in arms:
             timer = EventTimer(pool=2 * args.iters)
             for it in range(args.warmup + args.iters):
                 if it >= args.warmup:
@@ -85,13 +102,15 @@ def main():
             res["b200ar_frac_of_hbm_bound"] = round(bound_ms / res["b200ar_ms_per_step"], 3)
         if rank == 0:
             print(json.dumps(res), flush=True)
-        del model, ours, ref
+        del model, ours, ref, arms
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
     comm.close()
+    if ref_ar is not None:
+        ref_ar.close()
+    torch.cuda.synchronize()
     dist.barrier(group=gloo)
-    sys.stdout.flush()
-    os._exit(0)
+    dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -5,6 +5,8 @@ Per rank x [M, 3584] ~ N(0,1), W [8192, 3584] ~ N(0, 0.02), M in {16, 128, 1024,
   fused      one tcgen05 kernel, reduce-scatter pushed from the epilogue
   ours_split tcgen05 GEMM, then the b200ar all-reduce
   cublas_nccl torch.matmul, then NCCL all_reduce
+  cublas_ref  torch.matmul, then the reference's all-reduce kernel (unmodified,
+              its own API; even world sizes, when installed)
 and reports each against the roofline max(FLOPs / measured bf16 peak,
 2 (N-1)/N * bytes / 770 GB/s per direction).
 
@@ -27,6 +29,7 @@ sys.path.insert(0, ROOT)
 from b200ar import CustomAllreduce  # noqa: E402
 from b200ar.ops.gemm import check_errors, linear  # noqa: E402
 from b200ar.utils.timing import EventTimer, L2Flusher, max_over_ranks, percentile  # noqa: E402
+from reference_arm import ReferenceArm, reference_available  # noqa: E402
 
 NVLINK_GBS = 770.0
 
@@ -47,9 +50,12 @@ def main():
     comm = CustomAllreduce(group=gloo, device=dev, nccl_group=dist.group.WORLD, max_size=160 << 20)
     peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
         os.path.join(ROOT, "MEASURED_PEAKS.json")) else {"bf16_tflops": 1590.0}
-    flush = L2Flusher(dev)
+    flush = L2Flusher(dev, align_group=dist.group.WORLD)
     K, N = 3584, 8192
     rows = []
+    ref = None
+    if world > 1 and world % 2 == 0 and reference_available():
+        ref = ReferenceArm(rank, world, gloo, max(int(v) for v in args.ms.split(",")) * N * 2)
     for m in (int(v) for v in args.ms.split(",")):
         g = torch.Generator(device=dev).manual_seed(1234 + rank + m)
         x = torch.randn(m, K, generator=g, device=dev).to(torch.bfloat16)
@@ -61,6 +67,8 @@ def main():
             "ours_split": lambda: comm.all_reduce(linear(x, w, out=part), out=out),
             "cublas_nccl": lambda: dist.all_reduce(torch.matmul(x, w.t(), out=part)),
         }
+        if ref is not None:
+            impls["cublas_ref"] = lambda: ref.all_reduce(torch.matmul(x, w.t(), out=part), out)
         timer = EventTimer(pool=2 * len(impls) * args.iters)
         for it in range(args.warmup + args.iters):
             for name, fn in impls.items():
@@ -86,10 +94,11 @@ def main():
         if rank == 0:
             print(json.dumps(row), flush=True)
     comm.close()
+    if ref is not None:
+        ref.close()
     torch.cuda.synchronize()
     dist.barrier(group=gloo)
-    sys.stdout.flush()
-    os._exit(0)
+    dist.destroy_process_group()
 
 
 if __name__ == "__main__":
