@@ -79,23 +79,33 @@ def ref_rope(x, pos, rot: RotaryTable):
 _ATTN_WS: Dict[Tuple[int, int, int], Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = {}
 
 
-def decode_attention(q, k_cache, v_cache, seq_len, hq: int, hkv: int, out=None, splits: int = 0):
-    """q [B, hq, 128]; caches [B, L, hkv, 128]; seq_len int32 [B] -> out [B, hq * 128]."""
+def decode_attention(q, k_cache, v_cache, seq_len, hq: int, hkv: int, out=None, splits: int = 0,
+                     impl: str = "mma"):
+    """q [B, hq, 128]; caches [B, L, hkv, 128]; seq_len int32 [B] -> out [B, hq * 128].
+
+    ``impl`` "tc": tcgen05 tensor cores with TMA-fed K/V; "mma": mma.sync."""
     b = q.shape[0]
     if out is None:
         out = torch.empty(b, hq * 128, dtype=q.dtype, device=q.device)
     if q.device.type == "cpu":
         out.copy_(ref_decode_attention(q, k_cache, v_cache, seq_len, hq, hkv).to(out.dtype))
         return out
+    tc = impl == "tc"
     if splits <= 0:
-        splits = _C.attention_splits(b, hkv, k_cache.shape[1])
+        splits = (_C.attention_tc_splits if tc else _C.attention_splits)(b, hkv, k_cache.shape[1])
     key = (q.device.index or 0, b * hq * splits, b * hkv)
     if key not in _ATTN_WS:
         _ATTN_WS[key] = (torch.empty(b * hq * splits * 128, dtype=torch.float32, device=q.device),
                          torch.empty(b * hq * splits * 2, dtype=torch.float32, device=q.device),
                          torch.zeros(b * hkv, dtype=torch.int32, device=q.device))
     acc, ml, cnt = _ATTN_WS[key]
-    _C.decode_attention(q, k_cache, v_cache, seq_len, out, acc, ml, cnt, hq, hkv, splits, 1.0 / math.sqrt(128))
+    if tc:
+        from .gemm import error_word
+
+        _C.decode_attention_tc(q, k_cache, v_cache, seq_len, out, acc, ml, cnt, error_word(q.device), hq, hkv, splits,
+                               1.0 / math.sqrt(128))
+    else:
+        _C.decode_attention(q, k_cache, v_cache, seq_len, out, acc, ml, cnt, hq, hkv, splits, 1.0 / math.sqrt(128))
     return out
 
 

@@ -32,6 +32,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--len", type=int, default=2049)
     ap.add_argument("--batches", default="1,8,32,64")
+    ap.add_argument("--impl", default="tc,mma", help="comma list of kernels: tc (tcgen05 + TMA), mma (mma.sync)")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     torch.manual_seed(0)
@@ -41,20 +42,20 @@ def main():
     if os.path.exists(p):
         peaks = json.load(open(p))
     hq, hkv, L = 8, 1, args.len
-    for b in (int(v) for v in args.batches.split(",")):
+    for b, impl in ((int(v), i) for v in args.batches.split(",") for i in args.impl.split(",")):
         q = torch.randn(b, hq, 128, device=dev).to(torch.bfloat16)
         kc = torch.randn(b, L + 16, hkv, 128, device=dev).to(torch.bfloat16)
         vc = torch.randn_like(kc)
         seq = torch.full((b,), L, dtype=torch.int32, device=dev)
         out = torch.empty(b, hq * 128, dtype=torch.bfloat16, device=dev)
         for _ in range(args.warmup):
-            decode_attention(q, kc, vc, seq, hq, hkv, out=out)
+            decode_attention(q, kc, vc, seq, hq, hkv, out=out, impl=impl)
         err = (out.float() - ref_decode_attention(q, kc, vc, seq, hq, hkv)).abs().max().item()
         reps = 20
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             for _ in range(reps):
-                decode_attention(q, kc, vc, seq, hq, hkv, out=out)
+                decode_attention(q, kc, vc, seq, hq, hkv, out=out, impl=impl)
         g.replay()
         torch.cuda.synchronize()
         warm = []
@@ -69,11 +70,11 @@ def main():
         for _ in range(args.iters):
             flush()
             timer.start("cold")
-            decode_attention(q, kc, vc, seq, hq, hkv, out=out)
+            decode_attention(q, kc, vc, seq, hq, hkv, out=out, impl=impl)
             timer.stop("cold")
         cold = percentile(timer.times_ms()["cold"], 50) * 1e3
         kv_bytes = 2 * b * L * hkv * 128 * 2
-        row = {"batch": b, "seq_len": L, "hq": hq, "hkv": hkv, "max_abs_err": round(err, 4),
+        row = {"impl": impl, "batch": b, "seq_len": L, "hq": hq, "hkv": hkv, "max_abs_err": round(err, 4),
                "warm_us": round(percentile(warm, 50), 2), "cold_us": round(cold, 2),
                "cold_tbs": round(kv_bytes / (cold * 1e-6) / 1e12, 3)}
         if peaks.get("hbm_gbs"):

@@ -66,7 +66,10 @@ def main():
     if os.path.exists(pk):
         peaks = json.load(open(pk))
     for B in (int(b) for b in args.batches.split(",")):
-        model = TPLlamaDecoder(comm, cfg, batch=B, max_len=args.context + args.warmup + 2 * args.iters + 8)
+        # Every replay (and each capture's warm-up step) advances the position by
+        # one: room for all arms' steps past the prefilled context.
+        steps = 3 * (args.warmup + args.iters + 1)
+        model = TPLlamaDecoder(comm, cfg, batch=B, max_len=args.context + steps + 8)
         model.prefill_random(args.context)
         model.set_input((torch.randn(B, cfg.hidden, device=dev)).to(torch.bfloat16))
         ours = model.capture()

@@ -259,6 +259,8 @@ __global__ void __launch_bounds__(STHREADS, 1)
           // RoPE + KV write: block b is head b of [q heads | k heads | v heads].
           const RopeKvArgs& r = a.rope;
           const int p = r.pos[m];
+          // A position past the cache (or the rotary table) is skipped, never written.
+          if (p < 0 || p >= r.max_len) continue;
           uint2 w0, w1;
           if (b < r.hq + r.hkv) {
             float y0[4], y1[4];

@@ -73,6 +73,7 @@ __global__ void rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, const int*
                                __nv_bfloat16* __restrict__ v_cache, int hq, int hkv, int d, int max_len) {
   const int b = blockIdx.x, h = blockIdx.y, i = threadIdx.x, half = d / 2;
   const int p = pos[b];
+  if (p < 0 || p >= max_len) return;  // past the cache and the rotary table: nothing to write
   const int64_t row = static_cast<int64_t>(b) * (hq + 2 * hkv) * d;
   const float c = cos_t[static_cast<int64_t>(p) * half + i];
   const float s = sin_t[static_cast<int64_t>(p) * half + i];

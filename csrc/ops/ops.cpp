@@ -72,6 +72,34 @@ void register_ops(py::module& m) {
                                  reinterpret_cast<unsigned*>(done_count.data_ptr<int>()), b, hq, hkv,
                                  128, static_cast<int>(k_cache.size(1)), splits, static_cast<float>(scale), stream());
       });
+  m.def("attention_tc_splits", &b200ar::attention_tc_splits);
+  m.def(
+      "decode_attention_tc",
+      [stream](const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache, const at::Tensor& seq_len,
+               at::Tensor& out, at::Tensor& part_acc, at::Tensor& part_ml, at::Tensor& done_count, at::Tensor& err,
+               int hq, int hkv, int splits, double scale) {
+        for (const at::Tensor* t : {&q, &k_cache, &v_cache, static_cast<const at::Tensor*>(&out)})
+          TORCH_CHECK(t->is_cuda() && t->is_contiguous() && t->scalar_type() == at::kBFloat16,
+                      "decode attention takes contiguous bf16 CUDA tensors");
+        TORCH_CHECK(k_cache.dim() == 4 && v_cache.sizes() == k_cache.sizes() && k_cache.size(2) == hkv &&
+                        k_cache.size(3) == 128,
+                    "KV caches are [batch, max_len, kv_heads, 128]");
+        const int64_t b = q.size(0);
+        TORCH_CHECK(q.numel() == b * hq * 128 && out.numel() == b * hq * 128 && k_cache.size(0) == b,
+                    "q and out are [batch, hq * 128]");
+        TORCH_CHECK(seq_len.scalar_type() == at::kInt && seq_len.numel() >= b, "seq_len must be int32 [batch]");
+        TORCH_CHECK(part_acc.numel() >= b * hq * splits * 128 && part_ml.numel() >= b * hq * splits * 2,
+                    "attention workspace too small");
+        TORCH_CHECK(done_count.scalar_type() == at::kInt && done_count.numel() >= b * hkv,
+                    "attention counters must be int32 with one entry per (batch, KV head), zero at first use");
+        TORCH_CHECK(err.is_cuda() && err.scalar_type() == at::kInt, "err must be a CUDA int32 tensor");
+        const at::cuda::OptionalCUDAGuard guard(device_of(q));
+        b200ar::decode_attention_tc(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), seq_len.data_ptr<int>(),
+                                    out.data_ptr(), part_acc.data_ptr<float>(), part_ml.data_ptr<float>(),
+                                    reinterpret_cast<unsigned*>(done_count.data_ptr<int>()), err.data_ptr<int>(), b,
+                                    hq, hkv, 128, static_cast<int>(k_cache.size(1)), splits,
+                                    static_cast<float>(scale), stream());
+      });
   m.def(
       "silu_mul",
       [stream](const at::Tensor& gu, at::Tensor& y, int group) {

@@ -38,16 +38,24 @@ def test_rope_kv_writes_cache():
         assert torch.equal(vc[i, p], x[i, hq + hkv:])
 
 
-@pytest.mark.parametrize("b,hq,hkv,L", [(1, 8, 1, 2049), (8, 8, 1, 2049), (4, 8, 2, 300), (2, 4, 4, 100)])
-def test_decode_attention(b, hq, hkv, L):
+@pytest.mark.parametrize("impl", ["mma", "tc"])
+@pytest.mark.parametrize("b,hq,hkv,L", [(1, 8, 1, 2049), (8, 8, 1, 2049), (4, 8, 2, 300), (2, 4, 4, 100),
+                                        (3, 16, 1, 129), (64, 8, 1, 2049)])
+def test_decode_attention(b, hq, hkv, L, impl):
+    from b200ar.ops.gemm import check_errors
     from b200ar.ops.layers import decode_attention, ref_decode_attention
 
     q = torch.randn(b, hq, 128, device="cuda").to(torch.bfloat16)
     kc = torch.randn(b, L + 16, hkv, 128, device="cuda").to(torch.bfloat16)
     vc = torch.randn(b, L + 16, hkv, 128, device="cuda").to(torch.bfloat16)
-    seq = torch.tensor([L - (i % 3) for i in range(b)], dtype=torch.int32, device="cuda")
-    out = decode_attention(q, kc, vc, seq, hq, hkv)
+    # Cache rows past each sequence hold NaN: a kernel must never let them reach the output.
+    kc[:, L - 2:] = float("nan")
+    vc[:, L - 2:] = float("nan")
+    seq = torch.tensor([L - 2 - (i % 3) for i in range(b)], dtype=torch.int32, device="cuda")
+    out = decode_attention(q, kc, vc, seq, hq, hkv, impl=impl)
     ref = ref_decode_attention(q, kc, vc, seq, hq, hkv)
+    torch.cuda.synchronize()
+    check_errors()
     torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
 
 
@@ -58,8 +66,9 @@ def test_silu_mul():
     torch.testing.assert_close(silu_mul(gu).float(), ref_silu_mul(gu).float(), atol=2e-2, rtol=1e-2)
 
 
+@pytest.mark.parametrize("impl", ["mma", "tc"])
 @pytest.mark.parametrize("splits", [1, 3, 64])
-def test_decode_attention_merge_rearms(splits):
+def test_decode_attention_merge_rearms(splits, impl):
     """The last split CTA merges the partials and re-arms its counter: repeated
     eager calls and CUDA-graph replays must keep matching the reference."""
     from b200ar.ops.layers import decode_attention, ref_decode_attention
@@ -71,13 +80,13 @@ def test_decode_attention_merge_rearms(splits):
     seq = torch.tensor([L, L - 7, 1, 0], dtype=torch.int32, device="cuda")
     out = torch.empty(b, hq * 128, dtype=torch.bfloat16, device="cuda")
     for _ in range(3):
-        decode_attention(q, kc, vc, seq, hq, hkv, out=out, splits=splits)
+        decode_attention(q, kc, vc, seq, hq, hkv, out=out, splits=splits, impl=impl)
     ref = ref_decode_attention(q, kc, vc, seq, hq, hkv)
     torch.testing.assert_close(out.float()[:3], ref[:3], atol=2e-2, rtol=2e-2)
     assert torch.equal(out[3], torch.zeros_like(out[3]))  # empty sequence -> zeros
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        decode_attention(q, kc, vc, seq, hq, hkv, out=out, splits=splits)
+        decode_attention(q, kc, vc, seq, hq, hkv, out=out, splits=splits, impl=impl)
     for _ in range(3):
         q.copy_(torch.randn_like(q, dtype=torch.float32).to(torch.bfloat16))
         g.replay()
