@@ -21,10 +21,14 @@
 // probabilities, and its dimension's output accumulator, rescaled by
 // exp2(m_old - m_new) when a chunk raises the max.
 //
-// Splits and merge are those of the legacy kernel: CTA (b, kv head, split)
-// handles tokens [len * s / splits, len * (s + 1) / splits) and writes its
-// partial (o, max, sum); the CTA that finishes last merges the splits and
-// re-arms the arrival counter. Every wait is bounded (2 s): on expiry the
+// Pipelining: scores and output live in two TMEM buffers each and P in two
+// shared tiles, so the scores MMA of chunk c + 1 and the output MMA of chunk c
+// run while the softmax warps work on chunk c + 1, and the output of chunk c
+// is added once the softmax of chunk c + 1 is done.
+//
+// Splits: CTA (b, kv head, split) handles a run of whole 128-token chunks of
+// sequence b and writes its partial (o, max, sum); the CTA that finishes last
+// merges the splits and re-arms the arrival counter. Every wait is bounded (2 s): on expiry the
 // kernel records kAttnTimeout in `err`, drains its TMA copies, frees TMEM and
 // returns.
 //
@@ -56,10 +60,10 @@ constexpr uint32_t kHalfTile = kTChunk * 128;        // 128 rows x 128 B (64 dim
 constexpr uint32_t kStageBytes = 4 * kHalfTile;      // K lo, K hi, V lo, V hi
 constexpr uint32_t kQHalf = kTN * 128;               // 16 rows x 128 B: 2 KB
 constexpr uint32_t kPHalf = kTN * 128;               // 16 heads x 64 tokens: 2 KB
-constexpr size_t kTSmem = 1024 /*align*/ + kTStages * kStageBytes + 2 * kQHalf + 2 * kPHalf +
+constexpr size_t kTSmem = 1024 /*align*/ + kTStages * kStageBytes + 2 * kQHalf + 4 * kPHalf +
                           2 * 4 * kTN * sizeof(float) /*chunk max*/ + 4 * kTN * sizeof(float) /*sums*/ +
                           256 /*barriers*/;
-constexpr uint32_t kTmemCols = 32;       // scores at column 0, output chunk at column 16
+constexpr uint32_t kTmemCols = 64;       // two scores buffers, two output buffers
 constexpr int kAttnTimeout = 2;
 
 struct AttnTcParams {
@@ -84,24 +88,27 @@ __device__ __forceinline__ float warp_sum32(float v) {
   return v;
 }
 
+// G: query heads handled per KV head (8 or 16); the MMA N stays 16 (its
+// minimum at M = 128), columns G..15 of S and O are never read.
+template <int G>
 __global__ void __launch_bounds__(kTThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, AttnTcParams p) {
   extern __shared__ __align__(1024) uint8_t attn_tc_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(attn_tc_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sKV = smem;                                   // [stage][K lo, K hi, V lo, V hi]
-  uint8_t* sQ = sKV + kTStages * kStageBytes;            // [2][16 rows x 128 B]
-  uint8_t* sP = sQ + 2 * kQHalf;                         // [2][16 rows x 128 B]
-  float* red = reinterpret_cast<float*>(sP + 2 * kPHalf);  // [2][4][16] chunk max per warp
+  uint8_t* sQ = sKV + kTStages * kStageBytes;            // [2 halves][16 rows x 128 B]
+  uint8_t* sP = sQ + 2 * kQHalf;                         // [2 buffers][2 halves][16 rows x 128 B]
+  float* red = reinterpret_cast<float*>(sP + 4 * kPHalf);  // [2][4][16] chunk max per warp
   float* sums = red + 2 * 4 * kTN;                       // [4][16] final sums per warp
   uint64_t* full = reinterpret_cast<uint64_t*>(sums + 4 * kTN);
   uint64_t* empty = full + kTStages;
   uint64_t* qbar = empty + kTStages;
-  uint64_t* sfull = qbar + 1;
-  uint64_t* ofull = sfull + 1;
-  uint64_t* pready = ofull + 1;
-  uint64_t* oempty = pready + 1;
-  uint64_t* redbar = oempty + 1;
+  uint64_t* sfull = qbar + 1;    // [2]: scores of chunk c in TMEM buffer c & 1
+  uint64_t* ofull = sfull + 2;   // [2]: output of chunk c in TMEM buffer c & 1
+  uint64_t* pready = ofull + 2;  // [2]: P of chunk c written (S buffer c & 1 consumed)
+  uint64_t* oempty = pready + 2; // [2]: output buffer c & 1 consumed
+  uint64_t* redbar = oempty + 2;
   uint64_t* sumbar = redbar + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sumbar + 1);
   volatile int* s_err = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -110,8 +117,11 @@ __global__ void __launch_bounds__(kTThreads, 1)
   const int b = blockIdx.x, kh = blockIdx.y, sp = blockIdx.z;
   const int splits = p.splits, group = p.group;
   const int len = p.seq_len[b];
-  const int t0 = static_cast<int>((static_cast<int64_t>(len) * sp) / splits);
-  const int t1 = static_cast<int>((static_cast<int64_t>(len) * (sp + 1)) / splits);
+  // Splits cover whole chunks: the partial chunk is the sequence's last.
+  const int chunks = (len + kTChunk - 1) / kTChunk;
+  const int per = (chunks + splits - 1) / splits;
+  const int t0 = min(len, sp * per * kTChunk);
+  const int t1 = min(len, (sp + 1) * per * kTChunk);
   const int nch = (t1 - t0 + kTChunk - 1) / kTChunk;
   const int hq = p.hkv * group;
   const int head0 = b * hq + kh * group;
@@ -122,10 +132,12 @@ __global__ void __launch_bounds__(kTThreads, 1)
       sm100::mbar_init(&empty[i], 1);
     }
     sm100::mbar_init(qbar, 1);
-    sm100::mbar_init(sfull, 1);
-    sm100::mbar_init(ofull, 1);
-    sm100::mbar_init(pready, 4);
-    sm100::mbar_init(oempty, 4);
+    for (int i = 0; i < 2; ++i) {
+      sm100::mbar_init(&sfull[i], 1);
+      sm100::mbar_init(&ofull[i], 1);
+      sm100::mbar_init(&pready[i], 4);
+      sm100::mbar_init(&oempty[i], 4);
+    }
     sm100::mbar_init(redbar, 4);
     sm100::mbar_init(sumbar, 4);
     *s_err = 0;
@@ -142,7 +154,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + kTN;
+  // TMEM columns: scores buffers at 0 and 16, output buffers at 32 and 48.
+  auto tS = [&](int c) { return tmem + static_cast<uint32_t>((c & 1) * kTN); };
+  auto tO = [&](int c) { return tmem + static_cast<uint32_t>(2 * kTN + (c & 1) * kTN); };
+  auto sPb = [&](int c) { return sP + (c & 1) * 2 * kPHalf; };
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -176,73 +191,103 @@ __global__ void __launch_bounds__(kTThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // Order: scores of chunk c, then the output of chunk c - 1, so that the
+    // softmax of chunk c overlaps the output MMA of chunk c - 1.
     if (sm100::elect_one()) {
       constexpr uint32_t idesc_s = sm100::idesc_bf16_f32(kTChunk, kTN);           // A, B K-major
       constexpr uint32_t idesc_o = sm100::idesc_bf16_f32(kTD, kTN) | (1u << 15);  // A MN-major
+      auto issue_output = [&](int c) -> bool {
+        // P of chunk c written; output buffer c & 1 free (consumed for chunk c - 2).
+        if (!sm100::mbar_wait(&pready[c & 1], (c >> 1) & 1u)) return false;
+        if (c >= 2 && !sm100::mbar_wait(&oempty[c & 1], ((c - 2) >> 1) & 1u)) return false;
+        sm100::tc_fence_after();
+        const uint8_t* vt = sKV + (c % kTStages) * kStageBytes + 2 * kHalfTile;
+        const uint8_t* pb = sPb(c);
+        // 8 K-steps of 16 tokens. V^T is MN-major: 16 tokens = 2048 bytes
+        // further in the V tile; its second 64 dims are one half tile away.
+#pragma unroll
+        for (int k = 0; k < kTChunk / 16; ++k) {
+          const uint64_t da = sm100::smem_desc_mn_sw128(vt + k * 2048, kHalfTile, 1024);
+          const uint64_t db = sm100::smem_desc_sw128(pb + (k >> 2) * kPHalf) + 2 * (k & 3);
+          sm100::mma_bf16(tO(c), da, db, idesc_o, k > 0 ? 1u : 0u);
+        }
+        sm100::mma_commit(&ofull[c & 1]);
+        sm100::mma_commit(&empty[c % kTStages]);
+        return true;
+      };
       bool ok = nch == 0 || sm100::mbar_wait(qbar, 0);
       for (int c = 0; c < nch && ok && !*s_err; ++c) {
         const int st = c % kTStages;
-        const uint32_t ph = (c / kTStages) & 1u;
-        if (!sm100::mbar_wait(&full[st], ph)) {
+        if (!sm100::mbar_wait(&full[st], (c / kTStages) & 1u)) {
+          ok = false;
+          break;
+        }
+        // Scores buffer c & 1 was last read for chunk c - 2 (its P is written).
+        if (c >= 2 && !sm100::mbar_wait(&pready[c & 1], ((c - 2) >> 1) & 1u)) {
           ok = false;
           break;
         }
         sm100::tc_fence_after();
         const uint8_t* kt = sKV + st * kStageBytes;
-        const uint8_t* vt = kt + 2 * kHalfTile;
-        // Scores: 8 K-steps of 16 dims; dims 0-63 in the low half tiles, 64-127 in the high ones.
+        // 8 K-steps of 16 dims; dims 0-63 in the low half tiles, 64-127 in the high ones.
 #pragma unroll
         for (int k = 0; k < kTD / 16; ++k) {
           const uint64_t da = sm100::smem_desc_sw128(kt + (k >> 2) * kHalfTile) + 2 * (k & 3);
           const uint64_t db = sm100::smem_desc_sw128(sQ + (k >> 2) * kQHalf) + 2 * (k & 3);
-          sm100::mma_bf16(tS, da, db, idesc_s, k > 0 ? 1u : 0u);
+          sm100::mma_bf16(tS(c), da, db, idesc_s, k > 0 ? 1u : 0u);
         }
-        sm100::mma_commit(sfull);
-        if (!sm100::mbar_wait(pready, c & 1u) || (c > 0 && !sm100::mbar_wait(oempty, (c - 1) & 1u))) {
+        sm100::mma_commit(&sfull[c & 1]);
+        if (c >= 1 && !issue_output(c - 1)) {
           ok = false;
           break;
         }
-        sm100::tc_fence_after();
-        // Output: 8 K-steps of 16 tokens. V^T is MN-major: 16 tokens = 2048 bytes
-        // further in the V tile; its second 64 dims are one half tile away.
-#pragma unroll
-        for (int k = 0; k < kTChunk / 16; ++k) {
-          const uint64_t da = sm100::smem_desc_mn_sw128(vt + k * 2048, kHalfTile, 1024);
-          const uint64_t db = sm100::smem_desc_sw128(sP + (k >> 2) * kPHalf) + 2 * (k & 3);
-          sm100::mma_bf16(tO, da, db, idesc_o, k > 0 ? 1u : 0u);
-        }
-        sm100::mma_commit(ofull);
-        sm100::mma_commit(&empty[st]);
       }
+      if (ok && nch > 0 && !*s_err) ok = issue_output(nch - 1);
       if (!ok) *s_err = 1;
     }
   } else {
     // ------------------------------------------------------------ softmax + output
-    const int q4 = warp & 3;       // TMEM lane quarter of this warp
+    const int q4 = warp & 3;         // TMEM lane quarter of this warp
     const int row = q4 * 32 + lane;  // token of the chunk (scores), head dim (output)
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
-    float m[kTN], l[kTN], o[kTN];
+    float m[G], l[G], o[G], alpha_prev[G];
 #pragma unroll
-    for (int h = 0; h < kTN; ++h) m[h] = -INFINITY, l[h] = 0.f, o[h] = 0.f;
+    for (int h = 0; h < G; ++h) m[h] = -INFINITY, l[h] = 0.f, o[h] = 0.f, alpha_prev[h] = 0.f;
     bool ok = true;
+    // Adds the output MMA of chunk c (relative to that chunk's running max) to o.
+    auto accumulate = [&](int c, const float* alpha) -> bool {
+      if (!sm100::mbar_wait(&ofull[c & 1], (c >> 1) & 1u)) return false;
+      sm100::tc_fence_after();
+      uint32_t orr[G];
+      if constexpr (G == 16) sm100::tmem_ld_32x32b_x16(tO(c) + lane_off, orr);
+      else sm100::tmem_ld_32x32b_x8(tO(c) + lane_off, orr);
+      sm100::tmem_ld_wait();
+#pragma unroll
+      for (int h = 0; h < G; ++h) o[h] = o[h] * alpha[h] + __uint_as_float(orr[h]);
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&oempty[c & 1]);
+      return true;
+    };
     for (int c = 0; c < nch; ++c) {
-      if (!sm100::mbar_wait(sfull, c & 1u)) {
+      if (!sm100::mbar_wait(&sfull[c & 1], (c >> 1) & 1u)) {
         ok = false;
         break;
       }
       sm100::tc_fence_after();
-      uint32_t sr[kTN];
-      sm100::tmem_ld_32x32b_x16(tS + lane_off, sr);
+      uint32_t sr[G];
+      if constexpr (G == 16) sm100::tmem_ld_32x32b_x16(tS(c) + lane_off, sr);
+      else sm100::tmem_ld_32x32b_x8(tS(c) + lane_off, sr);
       sm100::tmem_ld_wait();
       const int tok = t0 + c * kTChunk + row;
       const bool valid = tok < t1;
-      float x[kTN];
+      float x[G];
 #pragma unroll
-      for (int h = 0; h < kTN; ++h) x[h] = (valid && h < group) ? __uint_as_float(sr[h]) * p.scale_log2 : -INFINITY;
+      for (int h = 0; h < G; ++h) x[h] = (valid && h < group) ? __uint_as_float(sr[h]) * p.scale_log2 : -INFINITY;
       // Chunk max per head over this warp's 32 tokens, then over the 4 warps.
       float* rb = red + (c & 1) * 4 * kTN;
 #pragma unroll
-      for (int h = 0; h < kTN; ++h) {
+      for (int h = 0; h < G; ++h) {
         const float mx = warp_max(x[h]);
         if (lane == h) rb[q4 * kTN + h] = mx;
       }
@@ -252,9 +297,9 @@ __global__ void __launch_bounds__(kTThreads, 1)
         ok = false;
         break;
       }
-      float alpha[kTN];
+      float alpha[G];
 #pragma unroll
-      for (int h = 0; h < kTN; ++h) {
+      for (int h = 0; h < G; ++h) {
         const float cm = fmaxf(fmaxf(rb[h], rb[kTN + h]), fmaxf(rb[2 * kTN + h], rb[3 * kTN + h]));
         const float mn = fmaxf(m[h], cm);
         alpha[h] = m[h] == -INFINITY ? 0.f : exp2f(m[h] - mn);
@@ -280,12 +325,14 @@ __global__ void __launch_bounds__(kTThreads, 1)
         }
       }
       // P^T as the K-major B operand: row h (head), K index = token `row`,
-      // 128-byte swizzle (16-byte chunk index XOR row % 8).
+      // 128-byte swizzle (16-byte chunk index XOR row % 8). Buffer c & 1 was
+      // last read by the output MMA of chunk c - 2, complete once that
+      // chunk's output was accumulated (previous iteration).
       {
-        uint8_t* pt = sP + (row >> 6) * kPHalf;
+        uint8_t* pt = sPb(c) + (row >> 6) * kPHalf;
         const int col = row & 63;
 #pragma unroll
-        for (int h = 0; h < kTN; ++h) {
+        for (int h = 0; h < G; ++h) {
           const uint32_t off = h * 128 + ((((col >> 3) ^ (h & 7)) << 4) | ((col & 7) * 2));
           *reinterpret_cast<__nv_bfloat16*>(pt + off) = __float2bfloat16_rn(x[h]);
         }
@@ -293,26 +340,25 @@ __global__ void __launch_bounds__(kTThreads, 1)
       sm100::fence_proxy_async_smem();
       sm100::tc_fence_before();
       __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(pready);
-      if (!sm100::mbar_wait(ofull, c & 1u)) {
+      if (lane == 0) sm100::mbar_arrive(&pready[c & 1]);
+      // The output of chunk c - 1 (its MMA overlapped this chunk's softmax).
+      if (c >= 1 && !accumulate(c - 1, alpha_prev)) {
         ok = false;
         break;
       }
-      sm100::tc_fence_after();
-      uint32_t orr[kTN];
-      sm100::tmem_ld_32x32b_x16(tO + lane_off, orr);
-      sm100::tmem_ld_wait();
 #pragma unroll
-      for (int h = 0; h < kTN; ++h) o[h] = o[h] * alpha[h] + __uint_as_float(orr[h]);
-      sm100::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(oempty);
+      for (int h = 0; h < G; ++h) alpha_prev[h] = alpha[h];
+    }
+    if (ok && nch > 0) {
+      // o is relative to the max before the last chunk: the last chunk's factor
+      // rescales it, then its own output adds in.
+      ok = accumulate(nch - 1, alpha_prev);
     }
     if (!ok) *s_err = 1;
     // Sum of probabilities per head over the 128 token threads.
     if (ok) {
 #pragma unroll
-      for (int h = 0; h < kTN; ++h) {
+      for (int h = 0; h < G; ++h) {
         const float sv = warp_sum32(l[h]);
         if (lane == h) sums[q4 * kTN + h] = sv;
       }
@@ -322,7 +368,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
     }
     if (ok) {
 #pragma unroll
-      for (int h = 0; h < kTN; ++h) {
+      for (int h = 0; h < G; ++h) {
         if (h >= group) break;
         const int64_t base = static_cast<int64_t>(head0 + h) * splits + sp;
         p.part_acc[base * kTD + row] = o[h];
@@ -458,13 +504,14 @@ void decode_attention_tc(const void* q, const void* k_cache, const void* v_cache
   const CUtensorMap tv = kv_map(v_cache, batch, max_len, hkv);
   AttnTcParams prm{seq_len, part_acc, part_ml, done_count, static_cast<__nv_bfloat16*>(out), err, hkv, group, splits,
                    scale * 1.4426950408889634f};
+  auto kern = group <= 8 ? attn_tc_kernel<8> : attn_tc_kernel<16>;
   static PerDeviceOnce smem_attr;
   smem_attr([&] {
-    B200AR_CUDA(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(kTSmem)));
+    for (auto k : {attn_tc_kernel<8>, attn_tc_kernel<16>})
+      B200AR_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kTSmem)));
   });
   const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>(hkv), static_cast<unsigned>(splits));
-  attn_tc_kernel<<<grid, kTThreads, kTSmem, s>>>(tq, tk, tv, prm);
+  kern<<<grid, kTThreads, kTSmem, s>>>(tq, tk, tv, prm);
   B200AR_CUDA(cudaGetLastError());
 }
 
