@@ -238,7 +238,6 @@ __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_lamport_cluster_ker
   __shared__ float red[32];
   __shared__ float s_part;  // this CTA's sum of squares of the current row slice
   __shared__ int s_fail;
-  const uint32_t gen = read_generation(a.ctx, &s_gen);
   const int C = static_cast<int>(cluster.num_blocks());
   const int crank = static_cast<int>(cluster.block_rank());
   const int group = static_cast<int>(blockIdx.x) / C, groups = static_cast<int>(gridDim.x) / C;
@@ -247,6 +246,21 @@ __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_lamport_cluster_ker
   const int plen = max(0, min(slice, a.hp - p0));
   const int r = a.ctx.rank;
   const int64_t row_bytes = static_cast<int64_t>(a.hp) * 16;
+  // The first row's input, residual and gamma packets are loaded before the
+  // generation is read, so their cold loads overlap (a decode step has one row
+  // per cluster).
+  uint4 x0[PPT], res0[PPT], gam[PPT];
+#pragma unroll
+  for (int k = 0; k < PPT; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    if (i < plen && group < a.rows) {
+      const int64_t idx = p0 + i;
+      x0[k] = ld_in(a.x + (static_cast<int64_t>(group) * a.hp + idx) * 16);
+      res0[k] = ld_in(a.res + (static_cast<int64_t>(group) * a.hp + idx) * 16);
+      gam[k] = ld_in(a.gamma + idx * 16);
+    }
+  }
+  const uint32_t gen = read_generation(a.ctx, &s_gen);
   const int64_t buf = static_cast<int64_t>(gen % kLamportBuffers) * N * a.lam_cap;
   char* dst[N];
   rotate_ptrs<N>(a.lam, r, dst);
@@ -256,7 +270,7 @@ __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_lamport_cluster_ker
       const int i = threadIdx.x + k * blockDim.x;
       if (i < plen) {
         const int64_t idx = p0 + i;
-        uint4 v = ld_in(a.x + (row * a.hp + idx) * 16);
+        uint4 v = row == group ? x0[k] : ld_in(a.x + (row * a.hp + idx) * 16);
         v.x = lamport_clean<__nv_bfloat16>(v.x);
         v.y = lamport_clean<__nv_bfloat16>(v.y);
         v.z = lamport_clean<__nv_bfloat16>(v.z);
@@ -274,32 +288,42 @@ __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_lamport_cluster_ker
   for (int64_t row = group; row < a.rows; row += groups) {
     const char* src = mine + row * row_bytes;
     // Bounded wait for every source's packets of this slice. All packets are
-    // loaded first, so the common case costs one round trip.
+    // loaded first, so the common case costs one round trip, and the polled
+    // values are the ones summed (no second load).
+    // Wide rows (PPT > 1) keep only the first packet's sources in registers
+    // and load the others again for the sum.
+    uint4 pv[1][N];
     bool ready[PPT][N];
 #pragma unroll
     for (int k = 0; k < PPT; ++k) {
       const int i = threadIdx.x + k * blockDim.x;
 #pragma unroll
-      for (int q = 0; q < N; ++q)
-        ready[k][q] = i >= plen || lamport_ready(ld_volatile16(src + static_cast<int64_t>(q) * a.lam_cap +
-                                                                static_cast<int64_t>(p0 + i) * 16));
+      for (int q = 0; q < N; ++q) {
+        uint4 t = make_uint4(0u, 0u, 0u, 0u);
+        if (i < plen) t = ld_volatile16(src + static_cast<int64_t>(q) * a.lam_cap + static_cast<int64_t>(p0 + i) * 16);
+        ready[k][q] = i >= plen || lamport_ready(t);
+        if (k == 0) pv[0][q] = t;
+      }
     }
 #pragma unroll
     for (int k = 0; k < PPT; ++k) {
       const int i = threadIdx.x + k * blockDim.x;
+      if (i >= plen) continue;
 #pragma unroll
       for (int q = 0; q < N; ++q) {
         if (ready[k][q]) continue;
         const char* pk = src + static_cast<int64_t>(q) * a.lam_cap + static_cast<int64_t>(p0 + i) * 16;
         const uint64_t start = global_ns();
         uint32_t spins = 0;
-        while (!lamport_ready(ld_volatile16(pk))) {
+        uint4 t;
+        while (!lamport_ready(t = ld_volatile16(pk))) {
           if ((++spins & 63u) == 0u && global_ns() - start > a.ctx.timeout_ns) {
             report_status(a.ctx.status, kStatusTimeout, r, q, blockIdx.x, gen, 0);
             s_fail = 1;
             break;
           }
         }
+        if (k == 0) pv[0][q] = t;
       }
     }
     const int failed = __syncthreads_or(s_fail);
@@ -313,12 +337,13 @@ __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_lamport_cluster_ker
       const int64_t idx = p0 + i;
       uint4 v[N];
 #pragma unroll
-      for (int q = 0; q < N; ++q) v[q] = ld_cg(src + static_cast<int64_t>(q) * a.lam_cap + idx * 16);
+      for (int q = 0; q < N; ++q)
+        v[q] = k == 0 ? pv[0][q] : ld_cg(src + static_cast<int64_t>(q) * a.lam_cap + idx * 16);
       float acc[8];
       unpack_set<__nv_bfloat16>(v[0], acc);
 #pragma unroll
       for (int q = 1; q < N; ++q) unpack_add<__nv_bfloat16>(v[q], acc);
-      unpack_add<__nv_bfloat16>(ld_in(a.res + (row * a.hp + idx) * 16), acc);
+      unpack_add<__nv_bfloat16>(row == group ? res0[k] : ld_in(a.res + (row * a.hp + idx) * 16), acc);
       const uint4 zp = pack<__nv_bfloat16>(acc);
       st_out(a.z + (row * a.hp + idx) * 16, zp);
       unpack_set<__nv_bfloat16>(zp, zf[k]);
@@ -348,7 +373,7 @@ __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_lamport_cluster_ker
       if (i >= plen) continue;
       const int64_t idx = p0 + i;
       float g[8];
-      unpack_set<__nv_bfloat16>(ld_in(a.gamma + idx * 16), g);
+      unpack_set<__nv_bfloat16>(gam[k], g);
 #pragma unroll
       for (int e = 0; e < 8; ++e) zf[k][e] = zf[k][e] * inv * g[e];
       st_out(a.y + (row * a.hp + idx) * 16, pack<__nv_bfloat16>(zf[k]));
