@@ -63,6 +63,7 @@ class CustomAllreduce:
         # Slot capacity: two-shot of max_size, or one-shot push of push_max_size.
         cap = max(
             _C.variant_slot_bytes(sel.VARIANTS["twoshot"], self.cfg.max_size, self.world),
+            _C.variant_slot_bytes(sel.VARIANTS["twoshot_push"], self.cfg.max_size, self.world),
             _C.variant_slot_bytes(sel.VARIANTS["oneshot_push"], self.cfg.push_max_size, self.world),
             _C.variant_slot_bytes(sel.VARIANTS["oneshot_pull"], self.cfg.max_size, self.world),
             4096,
@@ -226,7 +227,7 @@ class CustomAllreduce:
         if self._comm is None:
             # The CPU emulation implements the slot variants and the Lamport one-shot.
             cpu_ok = (sel.VARIANTS["oneshot_push"], sel.VARIANTS["oneshot_pull"], sel.VARIANTS["twoshot"],
-                      sel.VARIANTS["lamport"])
+                      sel.VARIANTS["twoshot_push"], sel.VARIANTS["lamport"])
             if v not in cpu_ok or (v == sel.VARIANTS["lamport"]
                                    and inp.numel() * inp.element_size() > self.lamport_capacity):
                 v = sel.VARIANTS["auto"]

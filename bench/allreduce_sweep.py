@@ -64,14 +64,14 @@ def main():
         y = torch.empty_like(x)
         packets = s // 16
         cands = []
-        for v in ("oneshot_push", "oneshot_pull", "twoshot", "lamport", "nvls"):
-            if v in ("oneshot_push", "oneshot_pull", "twoshot") and _C_slot(v, s, world) > comm.slot_capacity:
+        for v in ("oneshot_push", "oneshot_pull", "twoshot", "twoshot_push", "lamport", "nvls"):
+            if v in ("oneshot_push", "oneshot_pull", "twoshot", "twoshot_push") and _C_slot(v, s, world) > comm.slot_capacity:
                 continue
             if v == "lamport" and s > comm.lamport_capacity:
                 continue
             if v == "nvls" and (comm.nvls is None or s > comm.nvls.bytes):
                 continue
-            per = packets // world if v in ("twoshot", "nvls") else packets
+            per = packets // world if v in ("twoshot", "twoshot_push", "nvls") else packets
             resident = comm._comm.resident_ctas(sel.VARIANTS[v])
             for ctas in args.ctas:
                 if ctas > 1 and per // ctas < 32:

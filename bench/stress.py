@@ -229,7 +229,7 @@ def main():
 
     def t12():
         gen = torch.Generator().manual_seed(2024)
-        variants = ["auto", "auto", "lamport", "oneshot_push", "oneshot_pull", "twoshot"]
+        variants = ["auto", "auto", "lamport", "oneshot_push", "oneshot_pull", "twoshot", "twoshot_push"]
         big = torch.empty(args.max_random_bytes // 2, dtype=torch.bfloat16, device=dev)
         big.uniform_(-1, 1, generator=torch.Generator(device=dev).manual_seed(rank))
         out = torch.empty_like(big)
@@ -242,6 +242,8 @@ def main():
             if v == "lamport" and nbytes > comm.lamport_capacity:
                 v = "auto"
             if v == "oneshot_push" and nbytes * ws > comm.slot_capacity:
+                v = "auto"
+            if v == "twoshot_push" and 2 * (nbytes + 16 * ws) > comm.slot_capacity:
                 v = "auto"
             n = nbytes // 2
             ar(big[:n], out[:n], variant=v)

@@ -129,6 +129,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   variants["nccl"] = static_cast<int>(kNccl);
   variants["copy"] = static_cast<int>(kCopy);
   variants["lamport"] = static_cast<int>(kLamport);
+  variants["twoshot_push"] = static_cast<int>(kTwoshotPush);
   m.attr("VARIANTS") = variants;
 
   m.def("ar_rmsnorm_slot_bytes", &ar_rmsnorm_slot_bytes);

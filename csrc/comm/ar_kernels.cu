@@ -19,6 +19,7 @@ void launch_typed(int variant, int ctas, int threads, const ArArgs& a, cudaStrea
     case kOneshotPush: oneshot_push_kernel<T, N><<<ctas, threads, 0, s>>>(a); break;
     case kOneshotPull: oneshot_pull_kernel<T, N><<<ctas, threads, 0, s>>>(a); break;
     case kTwoshot: twoshot_kernel<T, N><<<ctas, threads, 0, s>>>(a); break;
+    case kTwoshotPush: twoshot_push_kernel<T, N><<<ctas, threads, 0, s>>>(a); break;
     case kRegistered: registered_kernel<T, N><<<ctas, threads, 0, s>>>(a); break;
     case kLamport: oneshot_lamport_kernel<T, N><<<ctas, threads, 0, s>>>(a); break;
     default: throw std::invalid_argument("unknown all-reduce variant " + std::to_string(variant));
@@ -75,6 +76,7 @@ const void* kernel_of(int variant) {
     case kOneshotPush: return reinterpret_cast<const void*>(&oneshot_push_kernel<T, N>);
     case kOneshotPull: return reinterpret_cast<const void*>(&oneshot_pull_kernel<T, N>);
     case kTwoshot: return reinterpret_cast<const void*>(&twoshot_kernel<T, N>);
+    case kTwoshotPush: return reinterpret_cast<const void*>(&twoshot_push_kernel<T, N>);
     case kRegistered: return reinterpret_cast<const void*>(&registered_kernel<T, N>);
     case kLamport: return reinterpret_cast<const void*>(&oneshot_lamport_kernel<T, N>);
     default: return nullptr;

@@ -13,6 +13,8 @@
 //    barrier, rotated pull-reduce from every peer.
 //  * twoshot (new): push-reduce-scatter, barrier, reduce own part, barrier,
 //    pull-all-gather. Moves 2(N-1)/N of the message per direction per rank.
+//  * twoshot_push (new): the same traffic with the reduced parts pushed to
+//    the peers while they are reduced, then a local copy.
 //  * registered    <-> pcie_allreduce_kernel (cu:261-276): pull directly from
 //    registered peer buffers. Adds the end barrier the reference lacks, so a
 //    rank cannot overwrite its input while a peer still reads it.
@@ -226,6 +228,115 @@ __global__ void __launch_bounds__(kArThreads) twoshot_kernel(ArArgs a) {
 #pragma unroll
         for (int k = 1; k < N; ++k)
           if (o < ln[k]) v[u][k] = ld_cg(peer[k] + (outbox + rb[k] + o) * 16);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int o = o0 + u * blockDim.x;
+#pragma unroll
+        for (int k = 1; k < N; ++k)
+          if (o < ln[k]) st_out(a.out + (ab[k] + o) * 16, v[u][k]);
+      }
+    }
+  }
+  finish_generation(a.ctx, gen);
+}
+
+// Two-shot with a pushed all-gather. Slot layout on every rank (in packets,
+// part = ceil(P / N)):
+//   [0, N*part)          reduce-scatter inbox, row q = rank q's copy of this rank's part
+//   [N*part, 2*N*part)   gathered parts, row p = rank p's reduced part
+// Phase 1 is the two-shot scatter. In phase 2 each rank reduces its part and
+// stores the result straight into row r of every peer's gathered area
+// (stores, not the pulls of twoshot_kernel's phase 3), so that the NVLink
+// transfer of the reduced part overlaps the reduction; phase 3 is a local copy
+// of the gathered rows to the output.
+template <typename T, int N>
+__global__ void __launch_bounds__(kArThreads) twoshot_push_kernel(ArArgs a) {
+  __shared__ uint32_t s_gen;
+  const uint32_t gen = read_generation(a.ctx, &s_gen);
+  const int slot = gen & 1u;
+  const int r = a.ctx.rank;
+  const int64_t P = a.packets;
+  const int64_t part = (P + N - 1) / N;
+  const int G = gridDim.x;
+  const int j = blockIdx.x;
+  B200AR_ENTRY_RANGE(static_cast<int64_t>(2 * N) * part * 16, a.slot_cap, 1u)
+
+  char* peer[N];  // peer[k] = slot base of rank (r + k) % N
+  rotate_ptrs<N>(a.slot[slot], r, peer);
+  int64_t ab[N];
+  int rb[N], ln[N];
+  int smax = 0;
+#pragma unroll
+  for (int k = 0; k < N; ++k) {
+    const int p = (r + k) % N;
+    const int64_t pb = part_begin(P, N, p);
+    const int64_t plen = part_begin(P, N, p + 1) - pb;
+    const int64_t sb = part_begin(plen, G, j);
+    rb[k] = static_cast<int>(sb);
+    ln[k] = static_cast<int>(part_begin(plen, G, j + 1) - sb);
+    ab[k] = pb + sb;
+    smax = ln[k] > smax ? ln[k] : smax;
+  }
+
+  // Phase 1: scatter (as twoshot_kernel).
+  constexpr int U = N >= 8 ? 1 : (8 + N - 1) / N;
+  const int64_t row = static_cast<int64_t>(r) * part;
+  for (int o0 = threadIdx.x; o0 < smax; o0 += U * blockDim.x) {
+    uint4 v[U][N];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int o = o0 + u * blockDim.x;
+#pragma unroll
+      for (int k = 0; k < N; ++k)
+        if (o < ln[k]) v[u][k] = ld_in(a.in + (ab[k] + o) * 16);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int o = o0 + u * blockDim.x;
+#pragma unroll
+      for (int k = 0; k < N; ++k)
+        if (o < ln[k]) st_cg(peer[k] + (row + rb[k] + o) * 16, v[u][k]);
+    }
+  }
+
+  bool ok = cta_barrier<N>(a.ctx, j, epoch_of(gen, 0));
+
+  // Phase 2: reduce own part, write it to the output and push it to every peer.
+  const int64_t gathered = static_cast<int64_t>(N) * part;
+  if (ok) {
+    char* mine = peer[0];
+    for (int o = threadIdx.x; o < ln[0]; o += blockDim.x) {
+      const int64_t rel = rb[0] + o;
+      uint4 v[N];
+#pragma unroll
+      for (int q = 0; q < N; ++q) v[q] = ld_cg(mine + (static_cast<int64_t>(q) * part + rel) * 16);
+      float acc[PackTraits<T>::kElems];
+      unpack_set<T>(v[0], acc);
+#pragma unroll
+      for (int q = 1; q < N; ++q) unpack_add<T>(v[q], acc);
+      const uint4 res = pack<T>(acc);
+      st_out(a.out + (ab[0] + o) * 16, res);
+#pragma unroll
+      for (int k = 1; k < N; ++k) st_cg(peer[k] + (gathered + row + rel) * 16, res);
+    }
+  }
+
+  ok = cta_barrier<N>(a.ctx, j, epoch_of(gen, 1)) && ok;
+
+  // Phase 3: copy the peers' reduced parts from the gathered rows.
+  if (ok) {
+    const char* mine = peer[0];
+    for (int o0 = threadIdx.x; o0 < smax; o0 += U * blockDim.x) {
+      uint4 v[U][N];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int o = o0 + u * blockDim.x;
+#pragma unroll
+        for (int k = 1; k < N; ++k) {
+          const int64_t prow = static_cast<int64_t>((r + k) % N) * part;
+          if (o < ln[k]) v[u][k] = ld_cg(mine + (gathered + prow + rb[k] + o) * 16);
+        }
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {

@@ -260,7 +260,7 @@ LaunchInfo Communicator::plan(int64_t bytes, int variant, int ctas, bool capturi
       if (v == kNvls && (nvls_ == nullptr || bytes > nvls_->bytes())) v = kTwoshot;
       if (v == kLamport && (lam_cap_ == 0 || bytes > lam_cap_)) v = kOneshotPush;
       // Fall back to the least demanding variant whose slot requirement fits.
-      if (v == kOneshotPush || v == kOneshotPull || v == kTwoshot) {
+      if (v == kOneshotPush || v == kOneshotPull || v == kTwoshot || v == kTwoshotPush) {
         if (variant_slot_bytes(v, bytes, world_) > slot_cap_) {
           if (variant_slot_bytes(kTwoshot, bytes, world_) <= slot_cap_) v = kTwoshot;
           else if (variant_slot_bytes(kOneshotPull, bytes, world_) <= slot_cap_) v = kOneshotPull;
@@ -280,7 +280,7 @@ int plan_ctas(int variant, int64_t bytes, int world, int requested, int resident
   if (variant == kOneshotPush || variant == kOneshotPull || variant == kRegistered || variant == kLamport) {
     const int64_t packets = bytes / 16;
     want = (packets + 2 * kArThreads - 1) / (2 * kArThreads);
-  } else if (variant == kTwoshot || variant == kNvls) {
+  } else if (variant == kTwoshot || variant == kTwoshotPush || variant == kNvls) {
     const int64_t part = bytes / 16 / std::max(world, 1);
     want = (part + kArThreads - 1) / kArThreads;
   } else {

@@ -75,7 +75,7 @@ struct SelectorEntry {
 // nor kMaxCTAs. 0 for variants that are not barrier kernels (copy, NCCL).
 int plan_ctas(int variant, int64_t bytes, int world, int requested, int resident);
 
-constexpr int kNumVariants = 9;
+constexpr int kNumVariants = 10;
 
 struct LaunchInfo {
   int variant = kAuto;

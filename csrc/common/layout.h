@@ -139,6 +139,8 @@ enum Variant : int {
   kNccl = 6,          // fall back to NCCL (handled by the Python layer)
   kCopy = 7,          // world size 1: plain copy
   kLamport = 8,       // push with in-band "not yet written" markers: no barrier, no fence
+  kTwoshotPush = 9,   // push-reduce-scatter, barrier, reduce own part and push it to every peer,
+                      // barrier, local copy of the gathered parts
 };
 
 // The one-shot Lamport variant keeps kLamportBuffers rotating buffers of
@@ -161,6 +163,10 @@ B200AR_HD int64_t variant_slot_bytes(int variant, int64_t bytes, int world) {
     case kTwoshot: {
       const int64_t part = (packets + world - 1) / world;
       return (world + 1) * part * 16;
+    }
+    case kTwoshotPush: {
+      const int64_t part = (packets + world - 1) / world;
+      return 2 * world * part * 16;  // inbox rows + gathered rows, one of each per source
     }
     default: return 0;
   }

@@ -226,7 +226,7 @@ void ShmComm::run(const char* in, char* out, int64_t P, int variant, int G) {
         }
         packet_store<T>(out + i * 16, acc);
       }
-    } else if (variant == kTwoshot) {
+    } else if (variant == kTwoshot || variant == kTwoshotPush) {
       const int64_t part = (P + N - 1) / N;
       auto sub = [&](int p, int64_t* pb, int64_t* sb, int64_t* sl) {
         *pb = part_begin(P, N, p);
@@ -244,20 +244,33 @@ void ShmComm::run(const char* in, char* out, int64_t P, int variant, int G) {
       if (!(ok = barrier(j, epoch_of(gen, 0)))) break;
       sub(r, &pb, &sb, &sl);
       char* mine = slotp(r);
+      const bool push = variant == kTwoshotPush;
+      const int64_t gathered = static_cast<int64_t>(N) * part;
       for (int64_t o = sb; o < sb + sl; ++o) {
         packet_set<T>(mine + o * 16, acc);
         for (int q = 1; q < N; ++q) packet_add<T>(mine + (static_cast<int64_t>(q) * part + o) * 16, acc);
         packet_store<T>(out + (pb + o) * 16, acc);
-        std::memcpy(mine + (static_cast<int64_t>(N) * part + o) * 16, out + (pb + o) * 16, 16);
+        if (push) {
+          // Reduced packet into row r of every peer's gathered area.
+          for (int k = 1; k < N; ++k)
+            std::memcpy(slotp((r + k) % N) + (gathered + static_cast<int64_t>(r) * part + o) * 16,
+                        out + (pb + o) * 16, 16);
+        } else {
+          std::memcpy(mine + (gathered + o) * 16, out + (pb + o) * 16, 16);
+        }
       }
       if (!(ok = barrier(j, epoch_of(gen, 1)))) break;
       for (int k = 1; k < N; ++k) {
         const int p = (r + k) % N;
         sub(p, &pb, &sb, &sl);
-        std::memcpy(out + (pb + sb) * 16, slotp(p) + (static_cast<int64_t>(N) * part + sb) * 16, sl * 16);
+        if (push)
+          std::memcpy(out + (pb + sb) * 16, mine + (gathered + static_cast<int64_t>(p) * part + sb) * 16, sl * 16);
+        else
+          std::memcpy(out + (pb + sb) * 16, slotp(p) + (gathered + sb) * 16, sl * 16);
       }
     } else {
-      throw std::invalid_argument("CPU backend supports variants push (1), pull (2), two-shot (3), Lamport (8)");
+      throw std::invalid_argument(
+          "CPU backend supports variants push (1), pull (2), two-shot (3), Lamport (8), two-shot push (9)");
     }
   }
   if (skip) --skip_;

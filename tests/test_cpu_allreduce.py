@@ -7,7 +7,7 @@ import torch.distributed as dist
 
 from dist_util import run_ranks
 
-VARIANTS = ["oneshot_push", "oneshot_pull", "twoshot", "lamport"]
+VARIANTS = ["oneshot_push", "oneshot_pull", "twoshot", "twoshot_push", "lamport"]
 
 
 def _bf16_1024x1024_fp32_oracle(rank, world):

@@ -16,7 +16,7 @@ if NGPU < 2:
     pytest.skip("needs at least two GPUs", allow_module_level=True)
 WORLD = min(NGPU, 8)
 
-VARIANTS = ["oneshot_push", "oneshot_pull", "twoshot", "lamport"]
+VARIANTS = ["oneshot_push", "oneshot_pull", "twoshot", "twoshot_push", "lamport"]
 
 
 def _oracle(x, world):
@@ -78,7 +78,7 @@ def _graph_replay(rank, world):
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        for variant in ("oneshot_push", "twoshot", "oneshot_pull", "lamport"):
+        for variant in ("oneshot_push", "twoshot", "twoshot_push", "oneshot_pull", "lamport"):
             comm.all_reduce(inp, mid, variant=variant)
             mid.mul_(1.0 / world)
             comm.all_reduce(mid, out, variant=variant)
