@@ -27,6 +27,25 @@ def load_lines(path: str) -> List[dict]:
     return out
 
 
+def sweep_of(result: dict) -> List[dict]:
+    """Per-size rows of a bench line: the detailed ``sweep`` (``--json-out``)
+    or, for a printed line, its compact ``rows`` (columns ``rows_cols``)."""
+    if "sweep" in result:
+        return result["sweep"]
+    cols = result.get("rows_cols")
+    if not cols:
+        return []
+    out = []
+    for r in result.get("rows", []):
+        d = {k: v for k, v in zip(cols, r) if v is not None}
+        if result.get("n_gpus", 1) > 1 and d.get("eager_p50_us"):
+            n, s = result["n_gpus"], d["bytes"]
+            d["busbw_gbs"] = s / (d["eager_p50_us"] * 1e-6) / 1e9 * 2 * (n - 1) / n
+            d["busbw_frac_of_nvlink"] = d["busbw_gbs"] / 770.0
+        out.append(d)
+    return out
+
+
 def _fmt_us(row: dict, mode: str) -> str:
     st = row.get(f"{mode}_us")
     p50 = row.get(f"{mode}_p50_us")
@@ -41,8 +60,8 @@ def render(result: dict, reference: Optional[dict] = None) -> str:
     if "unavailable" in result:
         return f"{result.get('impl', '?')}: unavailable ({result['unavailable']})\n"
     ref_by_size: Dict[int, dict] = {}
-    if reference and "sweep" in reference:
-        ref_by_size = {r["bytes"]: r for r in reference["sweep"]}
+    if reference:
+        ref_by_size = {r["bytes"]: r for r in sweep_of(reference)}
     head = ["bytes", "variant", "eager us p50 (p10-p90)", "graph us p50 (p10-p90)", "NCCL eager us",
             "NCCL / ours", "busbw GB/s", "of NVLink"]
     if ref_by_size:
@@ -54,7 +73,7 @@ def render(result: dict, reference: Optional[dict] = None) -> str:
         "| " + " | ".join(head) + " |",
         "|" + "---|" * len(head),
     ]
-    for row in result.get("sweep", []):
+    for row in sweep_of(result):
         s = row["bytes"]
         eager = row.get("eager_p50_us")
         nccl = row.get("nccl_eager_p50_us")
@@ -95,7 +114,7 @@ def main():
     args = ap.parse_args()
     ref = None
     if args.reference:
-        refs = [r for r in load_lines(args.reference) if "sweep" in r]
+        refs = [r for r in load_lines(args.reference) if sweep_of(r)]
         ref = refs[-1] if refs else None
     for res in load_lines(args.result):
         print(render(res, ref))

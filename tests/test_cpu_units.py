@@ -165,9 +165,11 @@ def test_render_md_tables(tmp_path):
     p = tmp_path / "r.json"
     p.write_text("NCCL version banner\n" + json.dumps(ours) + "\n")
     assert len(rm.load_lines(str(p))) == 1
-    # The committed TP8 result renders (older lines carry fewer fields).
-    committed = rm.load_lines(os.path.join(root, "profiles", "bench_tp8.json"))
-    assert committed and "| 268435456 |" in rm.render(committed[-1])
+    # Recorded TP8 lines render: a detailed one (per-size sweep) and a printed
+    # one (compact rows only).
+    for name in ("bench_line_tp8_detailed.json", "bench_line_tp8.json"):
+        committed = rm.load_lines(os.path.join(root, "tests", "data", name))
+        assert committed and "| 268435456 |" in rm.render(committed[-1], committed[-1]), name
 
 
 def test_rank_data_arena_bookkeeping():
