@@ -187,6 +187,8 @@ def summarize(per_call, sz_list, world, variant_of, graphs_on, nccl_on, nccl_gra
     return sweep, value, cross
 
 
+E2E_REPS = 5  # e2e samples per step of each message up to 1 MiB
+
 ROW_COLS = ["bytes", "variant", "eager_p50_us", "graph_p50_us", "nccl_eager_p50_us", "nccl_graph_p50_us",
             "e2e_p50_us"]
 
@@ -281,8 +283,11 @@ def run(args):
         host_out = {s: torch.empty_like(host_in[s]).pin_memory() for s in sz_list}
         dev_in = {s: torch.empty_like(inps[s]) for s in sz_list}
         e2e_times = {s: [] for s in sz_list}
+        # Small messages are sampled E2E_REPS times per step: their e2e time is
+        # tens of microseconds of host-side jitter around a short kernel.
+        reps = {s: E2E_REPS if s <= (1 << 20) else 1 for s in sz_list}
         for it in range(args.warmup + args.steps):
-            for s in sz_list:
+            for s in (s for s in sz_list for _ in range(reps[s])):
                 flush()
                 torch.cuda.synchronize()
                 if world > 1:
@@ -298,8 +303,8 @@ def run(args):
         e2e = {
             "value": round(geomean(list(e2e_p50.values())), 3),
             "unit": "us (geomean over sizes of p50, host clock, max over ranks)",
-            "h2d_bytes_per_step": int(sum(sz_list)),
-            "d2h_bytes_per_step": int(sum(sz_list)),
+            "h2d_bytes_per_step": int(sum(s * reps[s] for s in sz_list)),
+            "d2h_bytes_per_step": int(sum(s * reps[s] for s in sz_list)),
         }
 
     sweep, value, cross = summarize(per_call, sz_list, world, arm.variant, bool(graphs), with_nccl,
