@@ -40,7 +40,7 @@ _SKINNY: Dict[int, dict] = {}
 
 
 def _skinny_workspace(device, splits: int, m: int, n: int):
-    """Per-device decode-GEMM scratch: fp32 partials and zeroed arrival counters
+    """Per-device split-K scratch: fp32 partials and zeroed arrival counters
     (reused by every decode GEMM on that device; calls are stream-ordered)."""
     idx = torch.device(device).index or 0
     ws = _SKINNY.setdefault(idx, {})
@@ -58,7 +58,7 @@ def _skinny_workspace(device, splits: int, m: int, n: int):
 def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None, max_ctas: int = 0,
            skinny: Optional[bool] = None) -> torch.Tensor:
     """``x @ w.T`` (bf16). ``x``: [..., K]; ``w``: [N, K]. Rows <= 128 use the
-    stream-K decode kernel unless ``skinny=False``."""
+    split-K decode kernel unless ``skinny=False``."""
     shp = x.shape
     x2 = x.reshape(-1, shp[-1])
     if not x2.is_contiguous():
@@ -74,7 +74,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
         skinny = m <= 128
     if skinny:
         ws = _skinny_workspace(x.device, 1, m, n)
-        splits = _C.skinny_splits(n, x2.shape[1], ws["sms"], m)
+        splits = _C.skinny_splits(n, x2.shape[1], ws["sms"])
         ws = _skinny_workspace(x.device, splits, m, n)
         _C.gemm_skinny(x2, w, out2, ws["partials"], ws["counters"], error_word(x.device), splits)
     else:
@@ -101,7 +101,7 @@ def linear_silu_gate(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tenso
         gu = linear(x2, w, out=scratch)
         return silu_mul(gu.view(m, n), out=out, group=64)
     ws = _skinny_workspace(x.device, 1, m, n)
-    splits = _C.skinny_splits(n, x2.shape[1], ws["sms"], m)
+    splits = _C.skinny_splits(n, x2.shape[1], ws["sms"])
     ws = _skinny_workspace(x.device, splits, m, n)
     _C.gemm_skinny(x2, w, out.view(m, n // 2), ws["partials"], ws["counters"], error_word(x.device), splits, 1)
     return out
@@ -125,7 +125,7 @@ def linear_rope_kv(x: torch.Tensor, wqkv: torch.Tensor, pos: torch.Tensor, rot, 
         return
     x2 = x if x.is_contiguous() else x.contiguous()
     ws = _skinny_workspace(x.device, 1, m, n)
-    splits = _C.skinny_splits(n, x2.shape[1], ws["sms"], m)
+    splits = _C.skinny_splits(n, x2.shape[1], ws["sms"])
     ws = _skinny_workspace(x.device, splits, m, n)
     _C.gemm_skinny_rope_kv(x2, wqkv, pos, rot.cos, rot.sin, q_out, k_cache, v_cache, ws["partials"],
                            ws["counters"], error_word(x.device), splits, hq, hkv)

@@ -28,12 +28,13 @@ int gemm_grid(const gemm::Shape& s, int max_ctas);
 void gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int* err,
                cudaStream_t stream, int max_ctas = 0);
 
-// Decode GEMM for M <= 128 (swap-AB, stream-K: the (128-row weight block, K
-// block) units are split evenly over the grid). `partials` (fp32 [splits, M,
-// N], splits = skinny_splits(N, K, sms, M)) and `counters` (zeroed uint32
-// [ceil(N / 128)]) are always needed; calls that share them must be ordered on
-// one stream. `epilogue` 1 treats W as gate and up rows interleaved in groups
-// of 64 and writes silu(gate) * up to out[M, N / 2] (N a multiple of 128).
+// Decode GEMM for M <= 128 (swap-AB, split-K over `splits` CTAs per 128-row
+// weight block). `partials` (fp32 [splits, M, N]) and `counters` (zeroed
+// uint32 [ceil(N / 128)]) are needed when splits > 1; calls that share them
+// must be ordered on one stream. `epilogue` 1 treats W as gate and up rows
+// interleaved in groups of 64 and writes silu(gate) * up to out[M, N / 2]
+// (N a multiple of 128; partials and counters are needed for every split
+// count).
 // `epilogue` 2 treats W as the QKV projection (one 128-row block per head,
 // [q | k | v]) and, instead of writing `out`, rotates q and k (rotate-half
 // RoPE at pos[m]) and writes q to q_out[M, hq, 128] and k, v into the caches
@@ -47,9 +48,7 @@ struct RopeKvArgs {
   __nv_bfloat16* v_cache;
   int hq, hkv, max_len;
 };
-// Most CTAs that share one row block in the stream-K partition of a decode
-// GEMM of M rows: the partials must hold that many [M, N] fp32 slices.
-int skinny_splits(int64_t N, int64_t K, int sms, int64_t M = 1);
+int skinny_splits(int64_t N, int64_t K, int sms);
 void gemm_skinny(const void* x, const void* w, void* out, float* partials, unsigned* counters, int64_t M, int64_t N,
                  int64_t K, int splits, int* err, cudaStream_t stream, int epilogue = 0,
                  const RopeKvArgs* rope = nullptr);

@@ -1,21 +1,18 @@
 // Skinny (decode) GEMM for sm_100a: out[M, N] = x[M, K] * W[N, K]^T with M <= 128.
 //
-// Decode GEMMs stream the weights once and do little math per byte, so every
-// SM must stream the same share of them. The kernel swaps the operands (the
+// Decode GEMMs stream the weights once and do little math per byte, so the
+// work must be spread over every SM. The kernel swaps the operands (the
 // weight rows become the 128-wide UMMA M dimension, the padded batch the UMMA
-// N dimension, 16..128) and splits the U = (N / 128 row blocks) x (K / 64 K
-// blocks) units evenly over as many CTAs as fit on the device (stream-K): CTA
-// c takes units [c * per, (c + 1) * per), row block by row block.
+// N dimension, 16..128) and splits K over `splits` CTAs:
+//   CTA (b, s): weight rows [128 b, 128 b + 128), K blocks of split s.
 //   warp 0: TMA producer (W tile 128 x 64, x tile MP x 64, 6-stage ring)
-//   warp 1: tcgen05.mma issuer, one TMEM accumulator (128 lanes x MP columns)
-//           per row-block segment, two in turn
-//   warps 2-5: epilogue, thread = one weight row n, MP batch columns.
-// A row block covered by one CTA is written directly (bf16). Otherwise each
-// contributing CTA writes its fp32 partial to `partials[j][m][n]` (j = its
-// index among the block's contributors) and the contributor that arrives last
-// (per-block arrival counter) sums the partials in contributor order and
-// writes bf16, so results do not depend on arrival order. That CTA resets the
-// counter for the next call.
+//   warp 1: tcgen05.mma issuer, accumulator 128 lanes x MP columns in TMEM
+//   warps 0-3: epilogue, thread = one weight row n, MP batch columns.
+// With one split the bf16 result is written directly. Otherwise each CTA
+// writes its fp32 partial to `partials[s][m][n]`, and the last CTA of a row
+// block (per-block arrival counter) sums the partials in split order and
+// writes bf16, so results do not depend on arrival order. The counter is
+// reset by that last CTA for the next call.
 // Epilogue mode 1 (SiLU-gate): the weight rows hold gate and up projections
 // interleaved in groups of 64 (rows [128 b, 128 b + 64) = gate rows
 // [64 b, 64 b + 64), the next 64 rows = the matching up rows). The partials
@@ -45,8 +42,7 @@ namespace {
 constexpr int SBM = 128;
 constexpr int SBK = 64;
 constexpr int SSTAGES = 6;
-constexpr int STHREADS = 192;    // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
-constexpr int kRedThreads = 128; // epilogue threads
+constexpr int STHREADS = 128;
 
 template <int MP>
 struct SkinnyCfg {
@@ -54,24 +50,154 @@ struct SkinnyCfg {
   static constexpr uint32_t X_BYTES = MP * SBK * 2;
   static constexpr uint32_t STAGE = W_BYTES + X_BYTES;
   static constexpr size_t SMEM = SSTAGES * STAGE + 1024 + 256;
-  static constexpr uint32_t TMEM_COLS = 2 * MP < 32 ? 32 : 2 * MP;  // two accumulators
+  static constexpr uint32_t TMEM_COLS = MP < 32 ? 32 : MP;
 };
 
 struct SkinnyArgs {
   __nv_bfloat16* out;
-  float* partials;      // [max contributors per row block, M, N]
+  float* partials;      // [splits, M, N] when splits > 1
   unsigned* counters;   // [N / 128] arrival counters, zero between calls
   int M, N, K;
-  int nblocks, kblocks;
-  int per;              // stream-K units (row block x K block) per CTA
+  int nblocks, splits, kblocks;
   int epi;              // 0: out[M, N] = x W^T; 1: SiLU-gate over 64-row groups, out[M, N / 2]; 2: RoPE + KV
   RopeKvArgs rope;      // epi 2 only
 };
 
-// Sum of the `contrib` fp32 partials of row block b (in contributor order, so
-// the result does not depend on arrival order), then the epilogue; run by the
-// kRedThreads epilogue threads of the CTA that completed the block (tid 0..).
-__device__ __forceinline__ void reduce_block(const SkinnyArgs& a, int b, int contrib, int tid) {
+template <int MP>
+__global__ void __launch_bounds__(STHREADS, 1)
+    skinny_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                  SkinnyArgs a, int* err) {
+  using C = SkinnyCfg<MP>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sW = smem;
+  uint8_t* sX = smem + SSTAGES * C::W_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SSTAGES * C::STAGE);
+  uint64_t* empty = full + SSTAGES;
+  uint64_t* done = empty + SSTAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* s_err = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* s_last = const_cast<int*>(s_err) + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x % a.nblocks;
+  const int sp = blockIdx.x / a.nblocks;
+  const int kb0 = static_cast<int>((static_cast<int64_t>(a.kblocks) * sp) / a.splits);
+  const int kb1 = static_cast<int>((static_cast<int64_t>(a.kblocks) * (sp + 1)) / a.splits);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < SSTAGES; ++i) {
+      sm100::mbar_init(&full[i], 1);
+      sm100::mbar_init(&empty[i], 1);
+    }
+    sm100::mbar_init(done, 1);
+    *s_err = 0;
+    sm100::fence_barrier_init();
+    sm100::prefetch_tmap(&tmap_w);
+    sm100::prefetch_tmap(&tmap_x);
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(tmem_slot, C::TMEM_COLS);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (sm100::elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool issued[SSTAGES] = {};
+      uint32_t iphase[SSTAGES] = {};
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!sm100::mbar_wait(&empty[stage], phase ^ 1u)) {
+          *s_err = 1;
+          break;
+        }
+        sm100::mbar_arrive_expect_tx(&full[stage], C::STAGE);
+        sm100::tma_load_2d(sW + stage * C::W_BYTES, &tmap_w, &full[stage], kb * SBK, b * SBM);
+        sm100::tma_load_2d(sX + stage * C::X_BYTES, &tmap_x, &full[stage], kb * SBK, 0);
+        issued[stage] = true;
+        iphase[stage] = phase;
+        if (++stage == SSTAGES) stage = 0, phase ^= 1u;
+      }
+      for (int i = 0; i < SSTAGES; ++i)
+        if (issued[i]) sm100::mbar_wait(&full[i], iphase[i]);
+    }
+  } else if (warp == 1) {
+    if (sm100::elect_one()) {
+      constexpr uint32_t idesc = sm100::idesc_bf16_f32(SBM, MP);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!sm100::mbar_wait(&full[stage], phase)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        const uint64_t dw = sm100::smem_desc_sw128(sW + stage * C::W_BYTES);
+        const uint64_t dx = sm100::smem_desc_sw128(sX + stage * C::X_BYTES);
+#pragma unroll
+        for (int k = 0; k < SBK / 16; ++k) sm100::mma_bf16(tmem, dw + 2 * k, dx + 2 * k, idesc, (kb > kb0 || k > 0));
+        sm100::mma_commit(&empty[stage]);
+        if (++stage == SSTAGES) stage = 0, phase ^= 1u;
+      }
+      if (!ok) *s_err = 1;
+      sm100::mma_commit(done);  // also fires when no MMA was issued
+    }
+  }
+  __syncwarp();
+
+  // ---------------- epilogue: all 4 warps; thread = weight row n
+  const bool have = kb1 > kb0;
+  const bool ok = sm100::mbar_wait(done, 0);
+  if (!ok) *s_err = 1;
+  sm100::tc_fence_after();
+  const int n = b * SBM + warp * 32 + lane;
+  // Partial (or final) values leave TMEM 32 batch columns at a time.
+  constexpr int CH = MP < 32 ? MP : 32;
+  if (ok) {
+#pragma unroll 1
+    for (int c = 0; c < MP; c += CH) {
+      uint32_t r[32];
+      sm100::tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c, r);
+      sm100::tmem_ld_wait();
+      if (n < a.N) {
+#pragma unroll
+        for (int i = 0; i < CH; ++i) {
+          const int m = c + i;
+          if (m < a.M) {
+            const float v = have ? __uint_as_float(r[i]) : 0.f;
+            if (a.splits == 1 && a.epi == 0)
+              a.out[static_cast<int64_t>(m) * a.N + n] = __float2bfloat16_rn(v);
+            else
+              a.partials[(static_cast<int64_t>(sp) * a.M + m) * a.N + n] = v;
+          }
+        }
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+  if (!ok) {
+    if (threadIdx.x == 0) atomicExch(err, 1);
+    return;
+  }
+  if (a.splits == 1 && a.epi == 0) return;
+  // Split-K: the last CTA of this row block sums the partials in split order.
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) *s_last = atomicAdd(&a.counters[b], 1u) == static_cast<unsigned>(a.splits - 1);
+  __syncthreads();
+  if (!*s_last) return;
+  __threadfence();
   if (a.epi != 0) {
     // Paired epilogues: thread item = (row m, columns c .. c + 3 of this block
     // and the partner columns c + 64 .. c + 67); sums in split order, rounded
@@ -79,14 +205,14 @@ __device__ __forceinline__ void reduce_block(const SkinnyArgs& a, int b, int con
     constexpr int HALF = SBM / 2;
     const int64_t sstride = static_cast<int64_t>(a.M) * a.N;
     const int items = a.M * (HALF / 4);
-    for (int i0 = tid; i0 < items; i0 += 2 * kRedThreads) {
+    for (int i0 = threadIdx.x; i0 < items; i0 += 2 * STHREADS) {
       float4 lo[2], hi[2];
       int64_t off[2];
       int mm[2], cc[2];
       bool act[2];
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        const int it = i0 + j * kRedThreads;
+        const int it = i0 + j * STHREADS;
         mm[j] = it / (HALF / 4);
         cc[j] = (it % (HALF / 4)) * 4;
         act[j] = it < items && b * SBM + HALF + cc[j] < a.N;
@@ -94,7 +220,7 @@ __device__ __forceinline__ void reduce_block(const SkinnyArgs& a, int b, int con
         lo[j] = make_float4(0.f, 0.f, 0.f, 0.f);
         hi[j] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      for (int q = 0; q < contrib; ++q) {
+      for (int q = 0; q < a.splits; ++q) {
         float4 vl[2], vh[2];
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
@@ -174,26 +300,26 @@ __device__ __forceinline__ void reduce_block(const SkinnyArgs& a, int b, int con
     // block); four items and four splits of loads in flight, sums in split order.
     const int64_t sstride = static_cast<int64_t>(a.M) * a.N;
     const int items = a.M * (SBM / 4);
-    for (int i0 = tid; i0 < items; i0 += 4 * kRedThreads) {
+    for (int i0 = threadIdx.x; i0 < items; i0 += 4 * STHREADS) {
       float4 acc[4];
       int64_t off[4];
       bool on[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int it = i0 + j * kRedThreads;
+        const int it = i0 + j * STHREADS;
         const int m = it / (SBM / 4), c = (it % (SBM / 4)) * 4;
         const int col = b * SBM + c;
         on[j] = it < items && col < a.N;
         off[j] = static_cast<int64_t>(m) * a.N + col;
         acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      for (int q0 = 0; q0 < contrib; q0 += 4) {
+      for (int q0 = 0; q0 < a.splits; q0 += 4) {
         float4 v[4][4];
 #pragma unroll
         for (int q = 0; q < 4; ++q)
 #pragma unroll
           for (int j = 0; j < 4; ++j)
-            v[q][j] = (on[j] && q0 + q < contrib)
+            v[q][j] = (on[j] && q0 + q < a.splits)
                           ? __ldcg(reinterpret_cast<const float4*>(a.partials + (q0 + q) * sstride + off[j]))
                           : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
@@ -216,248 +342,13 @@ __device__ __forceinline__ void reduce_block(const SkinnyArgs& a, int b, int con
         }
     }
   }
-}
-
-// Stream-K partition of the U = nblocks x kblocks (row block, K block) units
-// over the grid: CTA c takes units [c * per, (c + 1) * per), row block by row
-// block. Every CTA streams the same number of weight bytes, whatever the shape.
-struct SkinnyPart {
-  int per;  // units per CTA
-  __host__ __device__ int first(int b, int kblocks) const { return (b * kblocks) / per; }
-  __host__ __device__ int last(int b, int kblocks) const { return ((b + 1) * kblocks - 1) / per; }
-};
-
-template <int MP>
-__global__ void __launch_bounds__(STHREADS, 1)
-    skinny_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-                  SkinnyArgs a, int* err) {
-  using C = SkinnyCfg<MP>;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sW = smem;
-  uint8_t* sX = smem + SSTAGES * C::W_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SSTAGES * C::STAGE);
-  uint64_t* empty = full + SSTAGES;
-  uint64_t* tfull = empty + SSTAGES;  // [2] accumulator of segment s ready
-  uint64_t* tempty = tfull + 2;       // [2] accumulator drained by the epilogue warps
-  uint64_t* esync = tempty + 2;       // epilogue warps meet (count 4)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(esync + 1);
-  volatile int* s_err = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* s_last = const_cast<int*>(s_err) + 1;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const SkinnyPart part{a.per};
-  const int U = a.nblocks * a.kblocks;
-  const int u0 = blockIdx.x * a.per;
-  const int u1 = min(U, u0 + a.per);
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < SSTAGES; ++i) {
-      sm100::mbar_init(&full[i], 1);
-      sm100::mbar_init(&empty[i], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      sm100::mbar_init(&tfull[i], 1);
-      sm100::mbar_init(&tempty[i], 4);
-    }
-    sm100::mbar_init(esync, 4);
-    *s_err = 0;
-    sm100::fence_barrier_init();
-    sm100::prefetch_tmap(&tmap_w);
-    sm100::prefetch_tmap(&tmap_x);
-  }
-  if (warp == 1) {
-    sm100::tmem_alloc(tmem_slot, C::TMEM_COLS);
-    sm100::tmem_relinquish();
-  }
-  sm100::tc_fence_before();
-  __syncthreads();
-  sm100::tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0) {
-    // ---------------- TMA producer: one weight tile and one activation tile per unit
-    if (sm100::elect_one()) {
-      int stage = 0;
-      uint32_t phase = 0;
-      bool issued[SSTAGES] = {};
-      uint32_t iphase[SSTAGES] = {};
-      for (int u = u0; u < u1 && !*s_err; ++u) {
-        const int b = u / a.kblocks, kb = u - b * a.kblocks;
-        if (!sm100::mbar_wait(&empty[stage], phase ^ 1u)) {
-          *s_err = 1;
-          break;
-        }
-        sm100::mbar_arrive_expect_tx(&full[stage], C::STAGE);
-        sm100::tma_load_2d(sW + stage * C::W_BYTES, &tmap_w, &full[stage], kb * SBK, b * SBM);
-        sm100::tma_load_2d(sX + stage * C::X_BYTES, &tmap_x, &full[stage], kb * SBK, 0);
-        issued[stage] = true;
-        iphase[stage] = phase;
-        if (++stage == SSTAGES) stage = 0, phase ^= 1u;
-      }
-      for (int i = 0; i < SSTAGES; ++i)
-        if (issued[i]) sm100::mbar_wait(&full[i], iphase[i]);
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer: one accumulator per segment (row block), two in turn
-    if (sm100::elect_one()) {
-      constexpr uint32_t idesc = sm100::idesc_bf16_f32(SBM, MP);
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      int seg = 0;
-      for (int s0 = u0; s0 < u1 && ok && !*s_err; ++seg) {
-        const int b = s0 / a.kblocks;
-        const int s1 = min(u1, (b + 1) * a.kblocks);
-        const int acc = seg & 1;
-        if (seg >= 2 && !sm100::mbar_wait(&tempty[acc], ((seg - 2) >> 1) & 1u)) {
-          ok = false;
-          break;
-        }
-        sm100::tc_fence_after();
-        const uint32_t d = tmem + static_cast<uint32_t>(acc * MP);
-        for (int u = s0; u < s1; ++u) {
-          if (!sm100::mbar_wait(&full[stage], phase)) {
-            ok = false;
-            break;
-          }
-          sm100::tc_fence_after();
-          const uint64_t dw = sm100::smem_desc_sw128(sW + stage * C::W_BYTES);
-          const uint64_t dx = sm100::smem_desc_sw128(sX + stage * C::X_BYTES);
-#pragma unroll
-          for (int k = 0; k < SBK / 16; ++k) sm100::mma_bf16(d, dw + 2 * k, dx + 2 * k, idesc, (u > s0 || k > 0));
-          sm100::mma_commit(&empty[stage]);
-          if (++stage == SSTAGES) stage = 0, phase ^= 1u;
-        }
-        if (!ok) break;
-        sm100::mma_commit(&tfull[acc]);
-        s0 = s1;
-      }
-      if (!ok) *s_err = 1;
-    }
-  } else {
-    // ---------------- epilogue warps 2..5: thread = weight row of the block
-    const int q4 = warp & 3;
-    const int tid = threadIdx.x - 64;
-    uint32_t ephase = 0;
-    auto group_sync = [&]() -> bool {  // the four epilogue warps meet (bounded)
-      __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(esync);
-      const bool r = sm100::mbar_wait(esync, ephase & 1u);
-      ++ephase;
-      return r;
-    };
-    constexpr int CH = MP < 32 ? MP : 32;
-    int seg = 0;
-    for (int s0 = u0; s0 < u1; ++seg) {
-      const int b = s0 / a.kblocks;
-      const int s1 = min(u1, (b + 1) * a.kblocks);
-      const int acc = seg & 1;
-      const int j = blockIdx.x - part.first(b, a.kblocks);                        // contributor index
-      const int contrib = part.last(b, a.kblocks) - part.first(b, a.kblocks) + 1;  // contributors of b
-      if (!sm100::mbar_wait(&tfull[acc], (seg >> 1) & 1u)) {
-        *s_err = 1;
-        break;
-      }
-      sm100::tc_fence_after();
-      const int n = b * SBM + q4 * 32 + lane;
-      const bool direct = contrib == 1 && a.epi == 0;
-#pragma unroll 1
-      for (int c = 0; c < MP; c += CH) {
-        uint32_t r[32];
-        sm100::tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + acc * MP + c, r);
-        sm100::tmem_ld_wait();
-        if (n < a.N) {
-#pragma unroll
-          for (int i = 0; i < CH; ++i) {
-            const int m = c + i;
-            if (m < a.M) {
-              const float v = __uint_as_float(r[i]);
-              if (direct)
-                a.out[static_cast<int64_t>(m) * a.N + n] = __float2bfloat16_rn(v);
-              else
-                a.partials[(static_cast<int64_t>(j) * a.M + m) * a.N + n] = v;
-            }
-          }
-        }
-      }
-      sm100::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(&tempty[acc]);
-      s0 = s1;
-      if (direct) continue;
-      // The contributor that completes row block b sums its partials.
-      __threadfence();
-      if (!group_sync()) {
-        *s_err = 1;
-        break;
-      }
-      if (tid == 0) *s_last = atomicAdd(&a.counters[b], 1u) == static_cast<unsigned>(contrib - 1);
-      if (!group_sync()) {
-        *s_err = 1;
-        break;
-      }
-      if (!*s_last) continue;
-      __threadfence();
-      reduce_block(a, b, contrib, tid);
-      if (tid == 0) a.counters[b] = 0;  // re-armed for the next call on this stream
-    }
-  }
-
-  sm100::tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    sm100::tc_fence_after();
-    sm100::tmem_dealloc(tmem, C::TMEM_COLS);
-  }
-  if (threadIdx.x == 0 && *s_err) atomicExch(err, 1);
-}
-
-// Grid and partition of a decode GEMM: as many CTAs as fit on the device at
-// once (shared memory allows two per SM for batches up to 16), capped by the
-// number of units; `maxc` is the most CTAs that share one row block.
-struct SkinnyPlan {
-  int grid, per, maxc;
-};
-
-// CTAs per SM the shared memory of the kernel for M rows allows.
-int skinny_ctas_per_sm(int64_t M) { return M <= 16 ? 2 : 1; }
-
-SkinnyPlan skinny_plan(int64_t M, int64_t N, int64_t K, int sms, int per_sm) {
-  const int64_t nblocks = (N + SBM - 1) / SBM;
-  const int64_t kblocks = (K + SBK - 1) / SBK;
-  const int64_t units = nblocks * kblocks;
-  const int64_t want = std::max<int64_t>(1, std::min<int64_t>(units, static_cast<int64_t>(per_sm) * sms));
-  SkinnyPlan p{};
-  p.per = static_cast<int>((units + want - 1) / want);
-  p.grid = static_cast<int>((units + p.per - 1) / p.per);
-  const SkinnyPart part{p.per};
-  int maxc = 1;
-  for (int64_t b = 0; b < nblocks; ++b)
-    maxc = std::max(maxc, part.last(static_cast<int>(b), static_cast<int>(kblocks)) -
-                              part.first(static_cast<int>(b), static_cast<int>(kblocks)) + 1);
-  p.maxc = maxc;
-  return p;
+  if (threadIdx.x == 0) a.counters[b] = 0;
 }
 
 template <int MP>
 void launch_skinny(const void* x, const void* w, void* out, float* partials, unsigned* counters, int64_t M, int64_t N,
-                   int64_t K, int maxc, int epi, const RopeKvArgs* rope, int* err, cudaStream_t stream) {
+                   int64_t K, int splits, int epi, const RopeKvArgs* rope, int* err, cudaStream_t stream) {
   using C = SkinnyCfg<MP>;
-  int dev = 0, sms = 0;
-  B200AR_CUDA(cudaGetDevice(&dev));
-  B200AR_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  auto kern = skinny_kernel<MP>;
-  static PerDeviceOnce smem_attr;
-  smem_attr([&] {
-    B200AR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM)));
-  });
-  // A smaller occupancy than planned only shrinks the grid (fewer contributors per block).
-  int occ = 0;
-  B200AR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, STHREADS, C::SMEM));
-  const SkinnyPlan plan = skinny_plan(M, N, K, sms, std::max(1, std::min(occ, skinny_ctas_per_sm(M))));
-  B200AR_CHECK(plan.maxc <= maxc, "decode GEMM partials sized for " << maxc << " contributors per row block, "
-                                                                     << plan.maxc << " needed");
   const CUtensorMap tw = make_tmap_bf16_2d(w, N, K, K, SBM, SBK);
   const CUtensorMap tx = make_tmap_bf16_2d(x, M, K, K, MP, SBK);
   SkinnyArgs a{};
@@ -469,17 +360,26 @@ void launch_skinny(const void* x, const void* w, void* out, float* partials, uns
   a.K = static_cast<int>(K);
   a.nblocks = static_cast<int>((N + SBM - 1) / SBM);
   a.kblocks = static_cast<int>((K + SBK - 1) / SBK);
-  a.per = plan.per;
+  a.splits = splits;
   a.epi = epi;
   if (rope) a.rope = *rope;
-  kern<<<plan.grid, STHREADS, C::SMEM, stream>>>(tw, tx, a, err);
+  auto kern = skinny_kernel<MP>;
+  static PerDeviceOnce smem_attr;
+  smem_attr([&] {
+    B200AR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM)));
+  });
+  kern<<<a.nblocks * splits, STHREADS, C::SMEM, stream>>>(tw, tx, a, err);
   B200AR_CUDA(cudaGetLastError());
 }
 
 }  // namespace
 
-int skinny_splits(int64_t N, int64_t K, int sms, int64_t M) {
-  return skinny_plan(M, N, K, sms, skinny_ctas_per_sm(M)).maxc;
+int skinny_splits(int64_t N, int64_t K, int sms) {
+  const int64_t nblocks = (N + SBM - 1) / SBM;
+  const int64_t kblocks = (K + SBK - 1) / SBK;
+  int64_t s = std::max<int64_t>(1, sms / nblocks);
+  s = std::min<int64_t>(s, std::max<int64_t>(1, kblocks / 2));  // at least two K blocks per split
+  return static_cast<int>(std::min<int64_t>(s, 16));
 }
 
 void gemm_skinny(const void* x, const void* w, void* out, float* partials, unsigned* counters, int64_t M, int64_t N,
@@ -491,8 +391,8 @@ void gemm_skinny(const void* x, const void* w, void* out, float* partials, unsig
   B200AR_CHECK(epilogue != 1 || N % SBM == 0, "the SiLU-gate epilogue needs N (gate + up rows) a multiple of 128");
   B200AR_CHECK(epilogue != 2 || (rope && N == static_cast<int64_t>(rope->hq + 2 * rope->hkv) * SBM),
                "the RoPE + KV epilogue needs its arguments and N = (hq + 2 hkv) * 128");
-  B200AR_CHECK(partials && counters, "the decode GEMM needs its partials and counters");
-  B200AR_CHECK(splits >= 1, "splits (contributors per row block) must be positive");
+  B200AR_CHECK((splits == 1 && epilogue == 0) || (partials && counters), "split-K needs partials and counters");
+  B200AR_CHECK(splits >= 1, "splits must be positive");
   if (M <= 16)
     launch_skinny<16>(x, w, out, partials, counters, M, N, K, splits, epilogue, rope, err, stream);
   else if (M <= 32)

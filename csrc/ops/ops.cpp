@@ -111,7 +111,7 @@ void register_ops(py::module& m) {
         b200ar::silu_mul(gu.data_ptr(), y.data_ptr(), gu.size(0), y.size(1), stream(), group);
       },
       py::arg("gate_up"), py::arg("y"), py::arg("group") = 0);
-  m.def("skinny_splits", &b200ar::skinny_splits, py::arg("n"), py::arg("k"), py::arg("sms"), py::arg("m") = 1);
+  m.def("skinny_splits", &b200ar::skinny_splits, py::arg("n"), py::arg("k"), py::arg("sms"));
   m.def(
       "gemm_skinny",
       [](const at::Tensor& x, const at::Tensor& w, at::Tensor& out, at::Tensor& partials, at::Tensor& counters,
@@ -122,7 +122,7 @@ void register_ops(py::module& m) {
         const int64_t out_cols = epilogue == 1 ? w.size(0) / 2 : w.size(0);
         TORCH_CHECK(x.size(1) == w.size(1) && out.size(0) == x.size(0) && out.size(1) == out_cols, "shape mismatch");
         TORCH_CHECK(partials.is_cuda() && partials.scalar_type() == at::kFloat &&
-                        partials.numel() >= splits * x.size(0) * w.size(0),
+                        partials.numel() >= (splits > 1 || epilogue ? splits * x.size(0) * w.size(0) : 0),
                     "partials must be a CUDA float32 tensor of splits * M * N elements");
         TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt &&
                         counters.numel() >= (w.size(0) + 127) / 128,
