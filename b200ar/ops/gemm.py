@@ -56,9 +56,10 @@ def _skinny_workspace(device, splits: int, m: int, n: int):
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None, max_ctas: int = 0,
-           skinny: Optional[bool] = None) -> torch.Tensor:
+           skinny: Optional[bool] = None, pair: bool = False) -> torch.Tensor:
     """``x @ w.T`` (bf16). ``x``: [..., K]; ``w``: [N, K]. Rows <= 128 use the
-    split-K decode kernel unless ``skinny=False``."""
+    split-K decode kernel unless ``skinny=False``; ``pair`` runs the CTA-pair
+    (cta_group::2) kernel for the other shapes."""
     shp = x.shape
     x2 = x.reshape(-1, shp[-1])
     if not x2.is_contiguous():
@@ -77,6 +78,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
         splits = _C.skinny_splits(n, x2.shape[1], ws["sms"])
         ws = _skinny_workspace(x.device, splits, m, n)
         _C.gemm_skinny(x2, w, out2, ws["partials"], ws["counters"], error_word(x.device), splits)
+    elif pair:
+        _C.gemm_bf16_2sm(x2, w, out2, error_word(x.device), max_ctas // 2)
     else:
         _C.gemm_bf16(x2, w, out2, error_word(x.device), max_ctas)
     return out.view(*shp[:-1], n)

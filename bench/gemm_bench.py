@@ -1,4 +1,5 @@
-"""tcgen05 GEMM throughput vs cuBLAS (torch.matmul) on the row-parallel
+"""tcgen05 GEMM throughput (single-CTA tiles and, above 128 rows, CTA-pair
+tiles) vs cuBLAS (torch.matmul) on the row-parallel
 down-projection shapes (x [M, 3584] @ W[8192, 3584]^T, M in {16, 128, 1024, 8192}) plus a
 square 8192^3 case. CUDA-event timing, L2 flushed before every call, p50.
 
@@ -39,14 +40,17 @@ def main():
         a = torch.randn(m, k, device=dev).to(torch.bfloat16)
         w = (0.02 * torch.randn(n, k, device=dev)).to(torch.bfloat16)
         out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
-        timer = EventTimer(pool=4 * args.iters)
+        names = ("tcgen05", "tcgen05_pair", "cublas") if m > 128 else ("tcgen05", "cublas")
+        timer = EventTimer(pool=2 * len(names) * args.iters)
         for it in range(args.warmup + args.iters):
-            for name in ("tcgen05", "cublas"):
+            for name in names:
                 flush()
                 if it >= args.warmup:
                     timer.start(name)
                 if name == "tcgen05":
                     linear(a, w, out=out)
+                elif name == "tcgen05_pair":
+                    linear(a, w, out=out, skinny=False, pair=True)
                 else:
                     torch.matmul(a, w.t(), out=out)
                 if it >= args.warmup:
@@ -55,12 +59,13 @@ def main():
         check_errors()
         flops = 2.0 * m * n * k
         row = {"M": m, "N": n, "K": k}
-        for name in ("tcgen05", "cublas"):
+        for name in names:
             us = percentile(t[name], 50) * 1e3
             row[f"{name}_us"] = round(us, 2)
             row[f"{name}_tflops"] = round(flops / (us * 1e-6) / 1e12, 1)
         if peaks.get("bf16_tflops"):
-            row["tcgen05_frac_of_measured_peak"] = round(row["tcgen05_tflops"] / peaks["bf16_tflops"], 3)
+            for name in names[:-1]:
+                row[f"{name}_frac_of_measured_peak"] = round(row[f"{name}_tflops"] / peaks["bf16_tflops"], 3)
         # Weight-streaming bound for small M: bytes of A, B and C over measured HBM bandwidth.
         if peaks.get("hbm_gbs"):
             bytes_ = 2 * (m * k + n * k + m * n)

@@ -10,6 +10,7 @@
 #include "../common/check.h"
 #include "../common/trace.h"
 #include "gemm.cuh"
+#include "gemm2sm.cuh"
 #include "gemm_api.h"
 
 namespace b200ar {
@@ -97,6 +98,47 @@ void gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int6
   });
   kern<<<gemm_grid(s, max_ctas), gemm::THREADS, gemm::smem_bytes<gemm::StoreC>(), stream>>>(ta, tb, s, epi, err);
   B200AR_CUDA(cudaGetLastError());
+}
+
+void gemm_bf16_2sm(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int* err,
+                   cudaStream_t stream, int max_pairs) {
+  const TraceRange trace("b200ar::gemm_bf16_2sm");
+  B200AR_CHECK(M > 0 && N > 0 && K > 0 && M < (1 << 30) && N < (1 << 30) && K < (1 << 30), "bad GEMM shape");
+  B200AR_CHECK(K % 8 == 0, "K must be a multiple of 8 (16-byte rows for TMA)");
+  B200AR_CHECK(N % 8 == 0 && reinterpret_cast<uintptr_t>(C) % 16 == 0, "C must have 16-byte aligned rows");
+  gemm2::Shape s{};
+  s.M = static_cast<int>(M);
+  s.N = static_cast<int>(N);
+  s.K = static_cast<int>(K);
+  s.tiles_m = static_cast<int>((M + gemm2::BM - 1) / gemm2::BM);
+  s.tiles_n = static_cast<int>((N + gemm2::BN - 1) / gemm2::BN);
+  s.kblocks = static_cast<int>((K + gemm2::BK - 1) / gemm2::BK);
+  const CUtensorMap ta = make_tmap_bf16_2d(A, M, K, K, 128, gemm2::BK);
+  const CUtensorMap tb = make_tmap_bf16_2d(B, N, K, K, 128, gemm2::BK);
+  static PerDeviceOnce smem_attr;
+  smem_attr([&] {
+    B200AR_CUDA(cudaFuncSetAttribute(gemm2::gemm2sm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(gemm2::SMEM_BYTES)));
+  });
+  int dev = 0;
+  B200AR_CUDA(cudaGetDevice(&dev));
+  int pairs = std::min(s.tiles_m * s.tiles_n, sm_count(dev) / 2);
+  if (max_pairs > 0) pairs = std::min(pairs, max_pairs);
+  pairs = std::max(pairs, 1);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(gemm2::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = gemm2::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  __nv_bfloat16* c = static_cast<__nv_bfloat16*>(C);
+  B200AR_CUDA(cudaLaunchKernelEx(&cfg, gemm2::gemm2sm_kernel, ta, tb, s, c, static_cast<int64_t>(N), err));
 }
 
 }  // namespace b200ar

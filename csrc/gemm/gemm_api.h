@@ -28,6 +28,11 @@ int gemm_grid(const gemm::Shape& s, int max_ctas);
 void gemm_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int* err,
                cudaStream_t stream, int max_ctas = 0);
 
+// The same product on CTA pairs (tcgen05 cta_group::2, 256 x 256 tiles,
+// clusters of 2): half the operand traffic per SM of the single-CTA kernel.
+void gemm_bf16_2sm(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int* err,
+                   cudaStream_t stream, int max_pairs = 0);
+
 // Decode GEMM for M <= 128 (swap-AB, split-K over `splits` CTAs per 128-row
 // weight block). `partials` (fp32 [splits, M, N]) and `counters` (zeroed
 // uint32 [ceil(N / 128)]) are needed when splits > 1; calls that share them

@@ -34,6 +34,20 @@ void register_ops(py::module& m) {
       },
       "C = A @ B^T with the tcgen05 GEMM (bf16 in/out, fp32 accumulate)", py::arg("a"), py::arg("b"), py::arg("c"),
       py::arg("err"), py::arg("max_ctas") = 0);
+  m.def(
+      "gemm_bf16_2sm",
+      [](const at::Tensor& a, const at::Tensor& b, at::Tensor& c, at::Tensor& err, int max_pairs) {
+        check_bf16_2d(a, "A");
+        check_bf16_2d(b, "B");
+        check_bf16_2d(c, "C");
+        TORCH_CHECK(a.size(1) == b.size(1) && c.size(0) == a.size(0) && c.size(1) == b.size(0), "shape mismatch");
+        TORCH_CHECK(err.is_cuda() && err.scalar_type() == at::kInt && err.numel() >= 1, "err must be a CUDA int32");
+        const at::cuda::OptionalCUDAGuard guard(device_of(a));
+        b200ar::gemm_bf16_2sm(a.data_ptr(), b.data_ptr(), c.data_ptr(), a.size(0), b.size(0), a.size(1),
+                              err.data_ptr<int>(), at::cuda::getCurrentCUDAStream().stream(), max_pairs);
+      },
+      "C = A @ B^T on CTA pairs (tcgen05 cta_group::2, 256 x 256 tiles)", py::arg("a"), py::arg("b"), py::arg("c"),
+      py::arg("err"), py::arg("max_pairs") = 0);
   auto stream = []() { return at::cuda::getCurrentCUDAStream().stream(); };
   m.def(
       "rmsnorm",

@@ -110,3 +110,22 @@ def test_linear_rope_kv_fused_epilogue(b, hq, hkv):
     torch.testing.assert_close(q1.float(), q2.float(), atol=2e-2, rtol=1e-2)
     torch.testing.assert_close(k1.float(), k2.float(), atol=2e-2, rtol=1e-2)
     assert torch.count_nonzero(k1) == torch.count_nonzero(k2)  # only positions `pos` were written
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 256, 64), (300, 520, 200), (1024, 8192, 3584), (8192, 1024, 1024),
+                                   (4096, 4096, 512)])
+def test_gemm_cta_pair_matches_fp32(m, n, k):
+    """The cta_group::2 kernel (256 x 256 tiles over two SMs) against fp32."""
+    from b200ar.ops.gemm import check_errors, linear
+
+    g = torch.Generator(device="cuda").manual_seed(m + 3 * n + k)
+    a = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+    w = (0.02 * torch.randn(n, k, generator=g, device="cuda")).to(torch.bfloat16)
+    for pairs in (0, 1, 3):  # persistent loop over tiles when the grid is capped
+        out = linear(a, w, skinny=False, pair=True, max_ctas=2 * pairs)
+        torch.cuda.synchronize()
+        check_errors()
+        ref = a.float() @ w.float().t()
+        err = (out.float() - ref).abs().max().item()
+        scale = ref.abs().max().item()
+        assert err <= 1e-2 * scale + 1e-2, (pairs, err, scale)
