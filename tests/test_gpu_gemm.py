@@ -21,9 +21,11 @@ def test_gemm_matches_fp32(m, n, k):
     a = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
     w = (0.02 * torch.randn(n, k, generator=g, device="cuda")).to(torch.bfloat16)
     out = linear(a, w)
+    out1 = linear(a, w, pair=False)  # single-CTA tiles (the fused GEMM + all-reduce main loop)
     torch.cuda.synchronize()
     check_errors()
     ref = a.float() @ w.float().t()
+    assert (out1.float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item() + 1e-2
     err = (out.float() - ref).abs().max().item()
     scale = ref.abs().max().item()
     assert err <= 1e-2 * scale + 1e-2, (err, scale)
