@@ -100,6 +100,21 @@ def build_table(measurements: Sequence[dict], slack: float = 0.0) -> List[Entry]
     return table
 
 
+def merge_partial_table(old: Sequence[Entry], new: Sequence[Entry], min_bytes: int) -> List[Entry]:
+    """Table of a sweep that started at ``min_bytes`` (``new``) merged into
+    the table of a full sweep (``old``): ``old`` keeps every size below
+    ``min_bytes`` (the entry that reached into the new range is cut at
+    ``min_bytes // 2``, the last size it was measured at), ``new`` serves the rest."""
+    keep: List[Entry] = []
+    for b, v, c in old:
+        if b < min_bytes:
+            keep.append((int(b), str(v), int(c)))
+        else:
+            keep.append((min_bytes // 2, str(v), int(c)))
+            break
+    return keep + [(int(b), str(v), int(c)) for b, v, c in new]
+
+
 def crossover_bytes(measurements: Sequence[dict], ours: str = "custom", theirs: str = "nccl") -> Optional[int]:
     """Smallest size above which ``theirs`` is at least as fast as ``ours`` for
     every larger measured size (None if ours wins everywhere)."""

@@ -37,6 +37,8 @@ def main():
     ap.add_argument("--tune", default="")
     ap.add_argument("--out", default="")
     ap.add_argument("--nvls", action="store_true")
+    ap.add_argument("--variants", default="oneshot_push,oneshot_pull,twoshot,twoshot_push,lamport,nvls",
+                    help="comma list of b200ar variants to time (NCCL is always timed)")
     ap.add_argument("--ctas", type=lambda v: [int(x) for x in v.split(",")], default=[1, 2, 4, 8, 16, 32, 64, 148, 296, 444])
     args = ap.parse_args()
 
@@ -64,7 +66,7 @@ def main():
         y = torch.empty_like(x)
         packets = s // 16
         cands = []
-        for v in ("oneshot_push", "oneshot_pull", "twoshot", "twoshot_push", "lamport", "nvls"):
+        for v in args.variants.split(","):
             if v in ("oneshot_push", "oneshot_pull", "twoshot", "twoshot_push") and _C_slot(v, s, world) > comm.slot_capacity:
                 continue
             if v == "lamport" and s > comm.lamport_capacity:
@@ -118,6 +120,8 @@ def main():
             if os.path.exists(args.tune):
                 with open(args.tune) as f:
                     tables = {int(k): [tuple(e) for e in v] for k, v in json.load(f).get("tables", {}).items()}
+            if args.min_bytes > 4096 and world in tables:
+                table = sel.merge_partial_table(tables[world], table, args.min_bytes)
             tables[world] = table
             sel.save_tables(args.tune, tables, {"how": "bench/allreduce_sweep.py, p50 of max over ranks"})
         print(json.dumps({"world": world, "table": table, "crossover_bytes": out["crossover_bytes"]}))

@@ -336,3 +336,13 @@ def test_bench_compact_rows():
     rows = bench.compact_rows(sweep, {4096: 40.123})
     assert bench.ROW_COLS[0] == "bytes" and len(bench.ROW_COLS) == 7
     assert rows == [[4096, "lamport", 11.0, 9.0, 20.0, None, 40.12], [8192, "twoshot", 12.0, None, None, None, None]]
+
+
+def test_partial_sweep_table_merge():
+    from b200ar.parallel.selector import merge_partial_table
+
+    old = [(16384, "lamport", 1), (131072, "lamport", 16), (4194304, "lamport", 296), (1 << 62, "twoshot", 64)]
+    new = [(2097152, "lamport", 64), (1 << 62, "twoshot_push", 148)]
+    got = merge_partial_table(old, new, 1 << 20)
+    assert got == [(16384, "lamport", 1), (131072, "lamport", 16), (524288, "lamport", 296),
+                   (2097152, "lamport", 64), (1 << 62, "twoshot_push", 148)]
