@@ -41,7 +41,13 @@ namespace {
 
 constexpr int SBM = 128;
 constexpr int SBK = 64;
-constexpr int SSTAGES = 6;
+// Ring depth per batch width: as many stages as fit in ~200 KB of shared
+// memory (11 at MP = 16, 6 at MP = 128), so that a CTA's whole K range of a
+// decode GEMM is usually in flight after one round trip.
+template <int MP>
+constexpr int skinny_stages() {
+  return (200 * 1024) / (SBM * SBK * 2 + MP * SBK * 2) > 12 ? 12 : (200 * 1024) / (SBM * SBK * 2 + MP * SBK * 2);
+}
 constexpr int STHREADS = 128;
 
 template <int MP>
@@ -49,7 +55,8 @@ struct SkinnyCfg {
   static constexpr uint32_t W_BYTES = SBM * SBK * 2;
   static constexpr uint32_t X_BYTES = MP * SBK * 2;
   static constexpr uint32_t STAGE = W_BYTES + X_BYTES;
-  static constexpr size_t SMEM = SSTAGES * STAGE + 1024 + 256;
+  static constexpr int STAGES = skinny_stages<MP>();
+  static constexpr size_t SMEM = STAGES * STAGE + 1024 + 256;
   static constexpr uint32_t TMEM_COLS = MP < 32 ? 32 : MP;
 };
 
@@ -71,10 +78,10 @@ __global__ void __launch_bounds__(STHREADS, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem;
-  uint8_t* sX = smem + SSTAGES * C::W_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SSTAGES * C::STAGE);
-  uint64_t* empty = full + SSTAGES;
-  uint64_t* done = empty + SSTAGES;
+  uint8_t* sX = smem + C::STAGES * C::W_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* done = empty + C::STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* s_err = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* s_last = const_cast<int*>(s_err) + 1;
@@ -86,7 +93,7 @@ __global__ void __launch_bounds__(STHREADS, 1)
   const int kb1 = static_cast<int>((static_cast<int64_t>(a.kblocks) * (sp + 1)) / a.splits);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < SSTAGES; ++i) {
+    for (int i = 0; i < C::STAGES; ++i) {
       sm100::mbar_init(&full[i], 1);
       sm100::mbar_init(&empty[i], 1);
     }
@@ -109,8 +116,8 @@ __global__ void __launch_bounds__(STHREADS, 1)
     if (sm100::elect_one()) {
       int stage = 0;
       uint32_t phase = 0;
-      bool issued[SSTAGES] = {};
-      uint32_t iphase[SSTAGES] = {};
+      bool issued[C::STAGES] = {};
+      uint32_t iphase[C::STAGES] = {};
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!sm100::mbar_wait(&empty[stage], phase ^ 1u)) {
           *s_err = 1;
@@ -121,9 +128,9 @@ __global__ void __launch_bounds__(STHREADS, 1)
         sm100::tma_load_2d(sX + stage * C::X_BYTES, &tmap_x, &full[stage], kb * SBK, 0);
         issued[stage] = true;
         iphase[stage] = phase;
-        if (++stage == SSTAGES) stage = 0, phase ^= 1u;
+        if (++stage == C::STAGES) stage = 0, phase ^= 1u;
       }
-      for (int i = 0; i < SSTAGES; ++i)
+      for (int i = 0; i < C::STAGES; ++i)
         if (issued[i]) sm100::mbar_wait(&full[i], iphase[i]);
     }
   } else if (warp == 1) {
@@ -143,7 +150,7 @@ __global__ void __launch_bounds__(STHREADS, 1)
 #pragma unroll
         for (int k = 0; k < SBK / 16; ++k) sm100::mma_bf16(tmem, dw + 2 * k, dx + 2 * k, idesc, (kb > kb0 || k > 0));
         sm100::mma_commit(&empty[stage]);
-        if (++stage == SSTAGES) stage = 0, phase ^= 1u;
+        if (++stage == C::STAGES) stage = 0, phase ^= 1u;
       }
       if (!ok) *s_err = 1;
       sm100::mma_commit(done);  // also fires when no MMA was issued
