@@ -80,10 +80,12 @@ _ATTN_WS: Dict[Tuple[int, int, int], Tuple[torch.Tensor, torch.Tensor, torch.Ten
 
 
 def decode_attention(q, k_cache, v_cache, seq_len, hq: int, hkv: int, out=None, splits: int = 0,
-                     impl: str = "mma"):
+                     impl: str = "tc"):
     """q [B, hq, 128]; caches [B, L, hkv, 128]; seq_len int32 [B] -> out [B, hq * 128].
 
-    ``impl`` "tc": tcgen05 tensor cores with TMA-fed K/V; "mma": mma.sync."""
+    ``impl`` "tc" (default): tcgen05 tensor cores with TMA-fed K/V; "mma": the
+    earlier mma.sync kernel, kept as the comparison point of
+    ``bench/attention_bench.py``."""
     b = q.shape[0]
     if out is None:
         out = torch.empty(b, hq * 128, dtype=q.dtype, device=q.device)
