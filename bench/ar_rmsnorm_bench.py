@@ -29,6 +29,7 @@ sys.path.insert(0, ROOT)
 
 from b200ar import CustomAllreduce  # noqa: E402
 from b200ar.utils.timing import EventTimer, L2Flusher, max_over_ranks, percentile  # noqa: E402
+sys.path.insert(0, os.path.join(ROOT, "bench"))
 from reference_arm import ReferenceArm, reference_available  # noqa: E402
 
 NVLINK_GBS = 770.0

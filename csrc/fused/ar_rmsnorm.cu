@@ -28,6 +28,7 @@
 #include "../comm/communicator.h"
 #include "../common/trace.h"
 #include "fused.h"
+#include "../common/pdl.h"
 
 namespace b200ar {
 
@@ -113,6 +114,8 @@ __device__ __forceinline__ void reduce_norm_row(const NormArgs& a, const char* s
 
 template <int N, int PPT>
 __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_oneshot_kernel(NormArgs a) {
+  pdl_wait();  // x comes from the previous kernel of the step
+  pdl_trigger();
   __shared__ uint32_t s_gen;
   __shared__ float red[32];
   const uint32_t gen = read_generation(a.ctx, &s_gen);
@@ -148,6 +151,8 @@ __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_oneshot_kernel(Norm
 // reduces, normalises and restores the markers (see oneshot_lamport_kernel).
 template <int N, int PPT>
 __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_lamport_kernel(NormArgs a) {
+  pdl_wait();  // x comes from the previous kernel of the step
+  pdl_trigger();
   __shared__ uint32_t s_gen;
   __shared__ float red[32];
   __shared__ int s_fail;
@@ -234,6 +239,8 @@ template <int N, int PPT>
 __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_lamport_cluster_kernel(NormArgs a) {
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
+  pdl_wait();  // x comes from the previous kernel of the step
+  pdl_trigger();
   __shared__ uint32_t s_gen;
   __shared__ float red[32];
   __shared__ float s_part;  // this CTA's sum of squares of the current row slice
@@ -391,6 +398,8 @@ __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_lamport_cluster_ker
 //   outbox [2][prow] rows : finished y rows, then z rows of this rank's part
 template <int N, int PPT>
 __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_twoshot_kernel(NormArgs a) {
+  pdl_wait();  // x comes from the previous kernel of the step
+  pdl_trigger();
   __shared__ uint32_t s_gen;
   __shared__ float red[32];
   const uint32_t gen = read_generation(a.ctx, &s_gen);
@@ -462,11 +471,11 @@ __global__ void __launch_bounds__(kMaxRowThreads) ar_rmsnorm_twoshot_kernel(Norm
 template <int N, int PPT>
 void launch_n(int kind, int ctas, int threads, const NormArgs& a, cudaStream_t s) {
   if (kind == 1)
-    ar_rmsnorm_twoshot_kernel<N, PPT><<<ctas, threads, 0, s>>>(a);
+    launch_pdl(ar_rmsnorm_twoshot_kernel<N, PPT>, dim3(ctas), dim3(threads), 0, s, 1, a);
   else if (kind == 2)
-    ar_rmsnorm_lamport_kernel<N, PPT><<<ctas, threads, 0, s>>>(a);
+    launch_pdl(ar_rmsnorm_lamport_kernel<N, PPT>, dim3(ctas), dim3(threads), 0, s, 1, a);
   else
-    ar_rmsnorm_oneshot_kernel<N, PPT><<<ctas, threads, 0, s>>>(a);
+    launch_pdl(ar_rmsnorm_oneshot_kernel<N, PPT>, dim3(ctas), dim3(threads), 0, s, 1, a);
 }
 
 template <int PPT>
@@ -488,19 +497,8 @@ void launch_ppt(int world, int kind, int ctas, int threads, const NormArgs& a, c
 // per cluster at a time.
 template <int N, int PPT>
 void launch_cluster_n(int C, int groups, int threads, const NormArgs& a, cudaStream_t s) {
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(C * groups));
-  cfg.blockDim = dim3(static_cast<unsigned>(threads));
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(C);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  B200AR_CUDA(cudaLaunchKernelEx(&cfg, ar_rmsnorm_lamport_cluster_kernel<N, PPT>, a));
+  launch_pdl(ar_rmsnorm_lamport_cluster_kernel<N, PPT>, dim3(static_cast<unsigned>(C * groups)),
+             dim3(static_cast<unsigned>(threads)), 0, s, C, a);
 }
 
 template <int PPT>

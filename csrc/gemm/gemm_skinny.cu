@@ -34,6 +34,7 @@
 #include "../common/trace.h"
 #include "gemm_api.h"
 #include "tcgen05.cuh"
+#include "../common/pdl.h"
 
 namespace b200ar {
 
@@ -111,6 +112,7 @@ __global__ void __launch_bounds__(STHREADS, 1)
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_trigger();  // the next kernel of a decode step may start its own set-up
 
   if (warp == 0) {
     if (sm100::elect_one()) {
@@ -118,7 +120,21 @@ __global__ void __launch_bounds__(STHREADS, 1)
       uint32_t phase = 0;
       bool issued[C::STAGES] = {};
       uint32_t iphase[C::STAGES] = {};
-      for (int kb = kb0; kb < kb1; ++kb) {
+      // Weights are never written by another kernel: the first ring's worth
+      // of weight tiles is requested before waiting for the previous kernel
+      // (which produces x), the matching activation tiles after it.
+      const int pre = min(kb1 - kb0, C::STAGES);
+      for (int i = 0; i < pre; ++i) {
+        sm100::mbar_arrive_expect_tx(&full[i], C::STAGE);
+        sm100::tma_load_2d(sW + i * C::W_BYTES, &tmap_w, &full[i], (kb0 + i) * SBK, b * SBM);
+        issued[i] = true;
+        iphase[i] = 0;
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) sm100::tma_load_2d(sX + i * C::X_BYTES, &tmap_x, &full[i], (kb0 + i) * SBK, 0);
+      stage = pre % C::STAGES;
+      phase = pre == C::STAGES ? 1u : 0u;
+      for (int kb = kb0 + pre; kb < kb1; ++kb) {
         if (!sm100::mbar_wait(&empty[stage], phase ^ 1u)) {
           *s_err = 1;
           break;
@@ -157,6 +173,7 @@ __global__ void __launch_bounds__(STHREADS, 1)
     }
   }
   __syncwarp();
+  pdl_wait();  // outputs, partials and counters are written only after the previous kernel completed
 
   // ---------------- epilogue: all 4 warps; thread = weight row n
   const bool have = kb1 > kb0;
@@ -375,7 +392,7 @@ void launch_skinny(const void* x, const void* w, void* out, float* partials, uns
   smem_attr([&] {
     B200AR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM)));
   });
-  kern<<<a.nblocks * splits, STHREADS, C::SMEM, stream>>>(tw, tx, a, err);
+  launch_pdl(kern, dim3(static_cast<unsigned>(a.nblocks * splits)), dim3(STHREADS), C::SMEM, stream, 1, tw, tx, a, err);
   B200AR_CUDA(cudaGetLastError());
 }
 

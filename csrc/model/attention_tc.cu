@@ -46,6 +46,7 @@
 #include "../common/trace.h"
 #include "../gemm/tcgen05.cuh"
 #include "model.h"
+#include "../common/pdl.h"
 
 namespace b200ar {
 
@@ -116,6 +117,11 @@ __global__ void __launch_bounds__(kTThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x, kh = blockIdx.y, sp = blockIdx.z;
   const int splits = p.splits, group = p.group;
+  // Everything this kernel reads may come from the previous kernel of the
+  // step (q and the new K/V row from the QKV projection): wait for it first;
+  // only the launch itself overlaps the previous kernel's tail.
+  pdl_wait();
+  pdl_trigger();
   const int len = p.seq_len[b];
   // Splits cover whole chunks: the partial chunk is the sequence's last.
   const int chunks = (len + kTChunk - 1) / kTChunk;
@@ -511,7 +517,7 @@ void decode_attention_tc(const void* q, const void* k_cache, const void* v_cache
       B200AR_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kTSmem)));
   });
   const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>(hkv), static_cast<unsigned>(splits));
-  kern<<<grid, kTThreads, kTSmem, s>>>(tq, tk, tv, prm);
+  launch_pdl(kern, grid, dim3(kTThreads), kTSmem, s, 1, tq, tk, tv, prm);
   B200AR_CUDA(cudaGetLastError());
 }
 
