@@ -77,7 +77,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
         skinny = m <= 128
     if skinny:
         ws = _skinny_workspace(x.device, 1, m, n)
-        splits = _C.skinny_splits(n, x2.shape[1], ws["sms"], m)
+        splits = _C.skinny_splits(n, x2.shape[1], ws["sms"])
         ws = _skinny_workspace(x.device, splits, m, n)
         _C.gemm_skinny(x2, w, out2, ws["partials"], ws["counters"], error_word(x.device), splits)
     elif pair:
@@ -106,7 +106,7 @@ def linear_silu_gate(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tenso
         gu = linear(x2, w, out=scratch)
         return silu_mul(gu.view(m, n), out=out, group=64)
     ws = _skinny_workspace(x.device, 1, m, n)
-    splits = _C.skinny_splits(n, x2.shape[1], ws["sms"], m)
+    splits = _C.skinny_splits(n, x2.shape[1], ws["sms"])
     ws = _skinny_workspace(x.device, splits, m, n)
     _C.gemm_skinny(x2, w, out.view(m, n // 2), ws["partials"], ws["counters"], error_word(x.device), splits, 1)
     return out
@@ -130,7 +130,7 @@ def linear_rope_kv(x: torch.Tensor, wqkv: torch.Tensor, pos: torch.Tensor, rot, 
         return
     x2 = x if x.is_contiguous() else x.contiguous()
     ws = _skinny_workspace(x.device, 1, m, n)
-    splits = _C.skinny_splits(n, x2.shape[1], ws["sms"], m)
+    splits = _C.skinny_splits(n, x2.shape[1], ws["sms"])
     ws = _skinny_workspace(x.device, splits, m, n)
     _C.gemm_skinny_rope_kv(x2, wqkv, pos, rot.cos, rot.sin, q_out, k_cache, v_cache, ws["partials"],
                            ws["counters"], error_word(x.device), splits, hq, hkv)

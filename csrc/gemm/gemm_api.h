@@ -53,8 +53,7 @@ struct RopeKvArgs {
   __nv_bfloat16* v_cache;
   int hq, hkv, max_len;
 };
-// Split count of the decode GEMM for M rows (the partials hold that many [M, N] slices).
-int skinny_splits(int64_t N, int64_t K, int sms, int64_t M = 1);
+int skinny_splits(int64_t N, int64_t K, int sms);
 void gemm_skinny(const void* x, const void* w, void* out, float* partials, unsigned* counters, int64_t M, int64_t N,
                  int64_t K, int splits, int* err, cudaStream_t stream, int epilogue = 0,
                  const RopeKvArgs* rope = nullptr);

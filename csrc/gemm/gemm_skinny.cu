@@ -45,24 +45,20 @@ constexpr int SBK = 64;
 // Ring depth per batch width: as many stages as fit in ~200 KB of shared
 // memory (11 at MP = 16, 6 at MP = 128), so that a CTA's whole K range of a
 // decode GEMM is usually in flight after one round trip.
-template <int MP, int NB>
+template <int MP>
 constexpr int skinny_stages() {
-  return (200 * 1024) / (NB * SBM * SBK * 2 + MP * SBK * 2) > 12 ? 12
-                                                                 : (200 * 1024) / (NB * SBM * SBK * 2 + MP * SBK * 2);
+  return (200 * 1024) / (SBM * SBK * 2 + MP * SBK * 2) > 12 ? 12 : (200 * 1024) / (SBM * SBK * 2 + MP * SBK * 2);
 }
 constexpr int STHREADS = 128;
 
-// NB: 128-row weight blocks per CTA (1, or 2 for wide batches, where the
-// activation tile is as large as a weight tile and sharing it between two
-// weight blocks halves its traffic).
-template <int MP, int NB>
+template <int MP>
 struct SkinnyCfg {
-  static constexpr uint32_t W_BYTES = NB * SBM * SBK * 2;
+  static constexpr uint32_t W_BYTES = SBM * SBK * 2;
   static constexpr uint32_t X_BYTES = MP * SBK * 2;
   static constexpr uint32_t STAGE = W_BYTES + X_BYTES;
-  static constexpr int STAGES = skinny_stages<MP, NB>();
+  static constexpr int STAGES = skinny_stages<MP>();
   static constexpr size_t SMEM = STAGES * STAGE + 1024 + 256;
-  static constexpr uint32_t TMEM_COLS = NB * MP < 32 ? 32 : NB * MP;
+  static constexpr uint32_t TMEM_COLS = MP < 32 ? 32 : MP;
 };
 
 struct SkinnyArgs {
@@ -70,17 +66,16 @@ struct SkinnyArgs {
   float* partials;      // [splits, M, N] when splits > 1
   unsigned* counters;   // [N / 128] arrival counters, zero between calls
   int M, N, K;
-  int nblocks, splits, kblocks;  // nblocks: groups of NB 128-row weight blocks
-  int nb128;                     // 128-row weight blocks
+  int nblocks, splits, kblocks;
   int epi;              // 0: out[M, N] = x W^T; 1: SiLU-gate over 64-row groups, out[M, N / 2]; 2: RoPE + KV
   RopeKvArgs rope;      // epi 2 only
 };
 
-template <int MP, int NB>
+template <int MP>
 __global__ void __launch_bounds__(STHREADS, 1)
     skinny_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                   SkinnyArgs a, int* err) {
-  using C = SkinnyCfg<MP, NB>;
+  using C = SkinnyCfg<MP>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem;
@@ -93,7 +88,7 @@ __global__ void __launch_bounds__(STHREADS, 1)
   int* s_last = const_cast<int*>(s_err) + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bs = blockIdx.x % a.nblocks;  // group of NB weight blocks
+  const int b = blockIdx.x % a.nblocks;
   const int sp = blockIdx.x / a.nblocks;
   const int kb0 = static_cast<int>((static_cast<int64_t>(a.kblocks) * sp) / a.splits);
   const int kb1 = static_cast<int>((static_cast<int64_t>(a.kblocks) * (sp + 1)) / a.splits);
@@ -131,7 +126,7 @@ __global__ void __launch_bounds__(STHREADS, 1)
       const int pre = min(kb1 - kb0, C::STAGES);
       for (int i = 0; i < pre; ++i) {
         sm100::mbar_arrive_expect_tx(&full[i], C::STAGE);
-        sm100::tma_load_2d(sW + i * C::W_BYTES, &tmap_w, &full[i], (kb0 + i) * SBK, bs * SBM * NB);
+        sm100::tma_load_2d(sW + i * C::W_BYTES, &tmap_w, &full[i], (kb0 + i) * SBK, b * SBM);
         issued[i] = true;
         iphase[i] = 0;
       }
@@ -145,7 +140,7 @@ __global__ void __launch_bounds__(STHREADS, 1)
           break;
         }
         sm100::mbar_arrive_expect_tx(&full[stage], C::STAGE);
-        sm100::tma_load_2d(sW + stage * C::W_BYTES, &tmap_w, &full[stage], kb * SBK, bs * SBM * NB);
+        sm100::tma_load_2d(sW + stage * C::W_BYTES, &tmap_w, &full[stage], kb * SBK, b * SBM);
         sm100::tma_load_2d(sX + stage * C::X_BYTES, &tmap_x, &full[stage], kb * SBK, 0);
         issued[stage] = true;
         iphase[stage] = phase;
@@ -169,11 +164,7 @@ __global__ void __launch_bounds__(STHREADS, 1)
         const uint64_t dw = sm100::smem_desc_sw128(sW + stage * C::W_BYTES);
         const uint64_t dx = sm100::smem_desc_sw128(sX + stage * C::X_BYTES);
 #pragma unroll
-        for (int j = 0; j < NB; ++j)  // block j: rows 128 j.. of the weight tile, accumulator columns MP j..
-#pragma unroll
-          for (int k = 0; k < SBK / 16; ++k)
-            sm100::mma_bf16(tmem + static_cast<uint32_t>(j * MP), dw + static_cast<uint64_t>(j) * (SBM * 128 / 16) + 2 * k,
-                            dx + 2 * k, idesc, (kb > kb0 || k > 0));
+        for (int k = 0; k < SBK / 16; ++k) sm100::mma_bf16(tmem, dw + 2 * k, dx + 2 * k, idesc, (kb > kb0 || k > 0));
         sm100::mma_commit(&empty[stage]);
         if (++stage == C::STAGES) stage = 0, phase ^= 1u;
       }
@@ -189,15 +180,14 @@ __global__ void __launch_bounds__(STHREADS, 1)
   const bool ok = sm100::mbar_wait(done, 0);
   if (!ok) *s_err = 1;
   sm100::tc_fence_after();
+  const int n = b * SBM + warp * 32 + lane;
   // Partial (or final) values leave TMEM 32 batch columns at a time.
   constexpr int CH = MP < 32 ? MP : 32;
   if (ok) {
 #pragma unroll 1
-    for (int jc = 0; jc < NB * MP; jc += CH) {
-      const int j = jc / MP, c = jc % MP;
-      const int n = (bs * NB + j) * SBM + warp * 32 + lane;
+    for (int c = 0; c < MP; c += CH) {
       uint32_t r[32];
-      sm100::tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + jc, r);
+      sm100::tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c, r);
       sm100::tmem_ld_wait();
       if (n < a.N) {
 #pragma unroll
@@ -228,14 +218,10 @@ __global__ void __launch_bounds__(STHREADS, 1)
   // Split-K: the last CTA of this row block sums the partials in split order.
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) *s_last = atomicAdd(&a.counters[bs], 1u) == static_cast<unsigned>(a.splits - 1);
+  if (threadIdx.x == 0) *s_last = atomicAdd(&a.counters[b], 1u) == static_cast<unsigned>(a.splits - 1);
   __syncthreads();
   if (!*s_last) return;
   __threadfence();
-#pragma unroll 1
-  for (int jb = 0; jb < NB; ++jb) {
-  const int b = bs * NB + jb;
-  if (b >= a.nb128) break;
   if (a.epi != 0) {
     // Paired epilogues: thread item = (row m, columns c .. c + 3 of this block
     // and the partner columns c + 64 .. c + 67); sums in split order, rounded
@@ -380,15 +366,14 @@ __global__ void __launch_bounds__(STHREADS, 1)
         }
     }
   }
-  }  // weight blocks of this group
-  if (threadIdx.x == 0) a.counters[bs] = 0;
+  if (threadIdx.x == 0) a.counters[b] = 0;
 }
 
-template <int MP, int NB>
+template <int MP>
 void launch_skinny(const void* x, const void* w, void* out, float* partials, unsigned* counters, int64_t M, int64_t N,
                    int64_t K, int splits, int epi, const RopeKvArgs* rope, int* err, cudaStream_t stream) {
-  using C = SkinnyCfg<MP, NB>;
-  const CUtensorMap tw = make_tmap_bf16_2d(w, N, K, K, NB * SBM, SBK);
+  using C = SkinnyCfg<MP>;
+  const CUtensorMap tw = make_tmap_bf16_2d(w, N, K, K, SBM, SBK);
   const CUtensorMap tx = make_tmap_bf16_2d(x, M, K, K, MP, SBK);
   SkinnyArgs a{};
   a.out = static_cast<__nv_bfloat16*>(out);
@@ -397,13 +382,12 @@ void launch_skinny(const void* x, const void* w, void* out, float* partials, uns
   a.M = static_cast<int>(M);
   a.N = static_cast<int>(N);
   a.K = static_cast<int>(K);
-  a.nblocks = static_cast<int>((N + NB * SBM - 1) / (NB * SBM));
-  a.nb128 = static_cast<int>((N + SBM - 1) / SBM);
+  a.nblocks = static_cast<int>((N + SBM - 1) / SBM);
   a.kblocks = static_cast<int>((K + SBK - 1) / SBK);
   a.splits = splits;
   a.epi = epi;
   if (rope) a.rope = *rope;
-  auto kern = skinny_kernel<MP, NB>;
+  auto kern = skinny_kernel<MP>;
   static PerDeviceOnce smem_attr;
   smem_attr([&] {
     B200AR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM)));
@@ -412,20 +396,15 @@ void launch_skinny(const void* x, const void* w, void* out, float* partials, uns
   B200AR_CUDA(cudaGetLastError());
 }
 
-// Weight blocks per CTA: two for batches wider than 32 rows.
-int skinny_group(int64_t M) { return M > 32 ? 2 : 1; }
-
 }  // namespace
 
-int skinny_splits(int64_t N, int64_t K, int sms, int64_t M) {
-  const int nb = skinny_group(M);
-  const int64_t groups = (N + nb * SBM - 1) / (nb * SBM);
+int skinny_splits(int64_t N, int64_t K, int sms) {
+  const int64_t nblocks = (N + SBM - 1) / SBM;
   const int64_t kblocks = (K + SBK - 1) / SBK;
-  int64_t s = std::max<int64_t>(1, sms / groups);
+  int64_t s = std::max<int64_t>(1, sms / nblocks);
   s = std::min<int64_t>(s, std::max<int64_t>(1, kblocks / 2));  // at least two K blocks per split
-  return static_cast<int>(std::min<int64_t>(s, 16 * nb));
+  return static_cast<int>(std::min<int64_t>(s, 16));
 }
-
 
 void gemm_skinny(const void* x, const void* w, void* out, float* partials, unsigned* counters, int64_t M, int64_t N,
                  int64_t K, int splits, int* err, cudaStream_t stream, int epilogue, const RopeKvArgs* rope) {
@@ -439,13 +418,13 @@ void gemm_skinny(const void* x, const void* w, void* out, float* partials, unsig
   B200AR_CHECK((splits == 1 && epilogue == 0) || (partials && counters), "split-K needs partials and counters");
   B200AR_CHECK(splits >= 1, "splits must be positive");
   if (M <= 16)
-    launch_skinny<16, 1>(x, w, out, partials, counters, M, N, K, splits, epilogue, rope, err, stream);
+    launch_skinny<16>(x, w, out, partials, counters, M, N, K, splits, epilogue, rope, err, stream);
   else if (M <= 32)
-    launch_skinny<32, 1>(x, w, out, partials, counters, M, N, K, splits, epilogue, rope, err, stream);
+    launch_skinny<32>(x, w, out, partials, counters, M, N, K, splits, epilogue, rope, err, stream);
   else if (M <= 64)
-    launch_skinny<64, 2>(x, w, out, partials, counters, M, N, K, splits, epilogue, rope, err, stream);
+    launch_skinny<64>(x, w, out, partials, counters, M, N, K, splits, epilogue, rope, err, stream);
   else
-    launch_skinny<128, 2>(x, w, out, partials, counters, M, N, K, splits, epilogue, rope, err, stream);
+    launch_skinny<128>(x, w, out, partials, counters, M, N, K, splits, epilogue, rope, err, stream);
 }
 
 }  // namespace b200ar

@@ -125,7 +125,7 @@ void register_ops(py::module& m) {
         b200ar::silu_mul(gu.data_ptr(), y.data_ptr(), gu.size(0), y.size(1), stream(), group);
       },
       py::arg("gate_up"), py::arg("y"), py::arg("group") = 0);
-  m.def("skinny_splits", &b200ar::skinny_splits, py::arg("n"), py::arg("k"), py::arg("sms"), py::arg("m") = 1);
+  m.def("skinny_splits", &b200ar::skinny_splits, py::arg("n"), py::arg("k"), py::arg("sms"));
   m.def(
       "gemm_skinny",
       [](const at::Tensor& x, const at::Tensor& w, at::Tensor& out, at::Tensor& partials, at::Tensor& counters,
