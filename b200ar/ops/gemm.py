@@ -38,6 +38,12 @@ def check_errors(device=None) -> None:
 
 _SKINNY: Dict[int, dict] = {}
 
+# Plain products up to this many rows run the split-K decode kernel; wider
+# ones the CTA-pair kernel, which was measured faster from 128 rows
+# (18.4 vs 25.6 us at 128 x 8192 x 1024, 32.8 vs 35.0 us at 128 x 8192 x 3584).
+# The fused SiLU-gate and RoPE + KV epilogues keep the decode kernel up to 128 rows.
+SKINNY_MAX_ROWS = 64
+
 
 def _skinny_workspace(device, splits: int, m: int, n: int):
     """Per-device split-K scratch: fp32 partials and zeroed arrival counters
@@ -57,10 +63,11 @@ def _skinny_workspace(device, splits: int, m: int, n: int):
 
 def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None, max_ctas: int = 0,
            skinny: Optional[bool] = None, pair: bool = True) -> torch.Tensor:
-    """``x @ w.T`` (bf16). ``x``: [..., K]; ``w``: [N, K]. Rows <= 128 use the
-    split-K decode kernel unless ``skinny=False``; other shapes run on CTA
-    pairs (tcgen05 cta_group::2, 256 x 256 tiles; 10-14 % faster than
-    single-CTA 128 x 256 tiles on B200), or on single CTAs with ``pair=False``.
+    """``x @ w.T`` (bf16). ``x``: [..., K]; ``w``: [N, K]. Up to
+    ``SKINNY_MAX_ROWS`` rows (or up to 128 with ``skinny=True``) use the split-K
+    decode kernel; other shapes run on CTA pairs (tcgen05 cta_group::2,
+    256 x 256 tiles; 10-14 % faster than single-CTA 128 x 256 tiles on B200),
+    or on single CTAs with ``pair=False``.
     ``max_ctas`` caps the persistent grid (rounded down to whole pairs)."""
     shp = x.shape
     x2 = x.reshape(-1, shp[-1])
@@ -74,7 +81,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
         out2.copy_((x2.float() @ w.float().t()).to(out2.dtype))
         return out.view(*shp[:-1], n)
     if skinny is None:
-        skinny = m <= 128
+        skinny = m <= SKINNY_MAX_ROWS
     if skinny:
         ws = _skinny_workspace(x.device, 1, m, n)
         splits = _C.skinny_splits(n, x2.shape[1], ws["sms"])

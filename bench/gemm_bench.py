@@ -40,7 +40,7 @@ def main():
         a = torch.randn(m, k, device=dev).to(torch.bfloat16)
         w = (0.02 * torch.randn(n, k, device=dev)).to(torch.bfloat16)
         out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
-        names = ("tcgen05", "tcgen05_pair", "cublas") if m > 128 else ("tcgen05", "cublas")
+        names = ("tcgen05", "tcgen05_pair", "cublas") if m >= 64 else ("tcgen05", "cublas")
         timer = EventTimer(pool=2 * len(names) * args.iters)
         for it in range(args.warmup + args.iters):
             for name in names:
